@@ -1,0 +1,77 @@
+"""emberllm_b200 — emberllm's token loop (decode + prefill of Q8_0/Q4_0 LLaMA-family
+decoders) on NVIDIA B200, behind emberllm's own C API.
+
+The product is the C-ABI library ``libember_b200.so`` (C11 host code + sm_100a
+CUDA kernels, built by ``make -C emberllm_b200``). This package is its Python
+face and mirrors emberllm's ctypes ``Ember`` class
+(bindings/python/emberllm.py:112-201) for the parts on the token loop: load a
+model, create a run state, prefill, forward, and greedy generation over token
+ids. Text tokenization stays with emberllm's tokenizer (host code outside the
+token loop), so this mirror works on ids.
+"""
+import ctypes
+
+from . import _lib as _libmod
+from ._lib import EmberHeader, cuda_available, load
+
+__all__ = ["Ember", "EmberHeader", "cuda_available", "load"]
+
+
+class Ember:
+    """A loaded model and one run state (mirrors emberllm's Python ``Ember``)."""
+
+    def __init__(self, path, ctx=0, kv_fp16=False):
+        self.lib = load()
+        self.m = self.lib.ember_model_load(str(path).encode())
+        if not self.m:
+            raise RuntimeError(f"failed to load model: {path}")
+        self.header = self.lib.ember_model_header(self.m).contents
+        self.st = self.lib.ember_state_new_ex(self.m, int(ctx), 1 if kv_fp16 else 0)
+        maxs = self.header.max_seq_len
+        self.ctx = maxs if ctx <= 0 or ctx > maxs else ctx
+        self.vocab = self.header.vocab_size
+
+    # -- token loop --------------------------------------------------------
+    def forward(self, tok, pos):
+        """Logits (a ctypes float array view of vocab_size) after token ``tok`` at ``pos``."""
+        return self.lib.ember_forward(self.m, self.st, int(tok), int(pos))
+
+    def prefill(self, ids, start=0):
+        arr = (ctypes.c_int * len(ids))(*ids)
+        return self.lib.ember_prefill(self.m, self.st, arr, len(ids), int(start))
+
+    def logits_list(self, ptr):
+        return [ptr[i] for i in range(self.vocab)]
+
+    def greedy(self, first_tok, pos, n):
+        """n greedy steps on the device; returns the n chosen token ids."""
+        out = (ctypes.c_int * n)()
+        self.lib.ember_forward_greedy(self.m, self.st, int(first_tok), int(pos), int(n), out)
+        return list(out)
+
+    def generate_ids(self, prompt_ids, max_tokens=128):
+        """Greedy continuation of ``prompt_ids`` (ids in, ids out), as the
+        reference's generate loop with temperature 0 (ref src/main.c:189-206)."""
+        logits = self.prefill(prompt_ids)
+        best = max(range(self.vocab), key=lambda i: (logits[i], -i))
+        if max_tokens <= 1:
+            return [best][:max_tokens]
+        return [best] + self.greedy(best, len(prompt_ids), max_tokens - 1)
+
+    # -- lifetime ----------------------------------------------------------
+    def close(self):
+        if getattr(self, "st", None):
+            self.lib.ember_state_free(self.st)
+            self.st = None
+        if getattr(self, "m", None):
+            self.lib.ember_model_free(self.m)
+            self.m = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        self.close()

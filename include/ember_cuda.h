@@ -1,0 +1,133 @@
+/* ember_cuda.h — the thin C-ABI shim between the C11 host code and the sm_100a
+ * kernels, plus the library's extension entry points.
+ *
+ * None of these functions has a counterpart in emberllm (which has no GPU
+ * path); they are what the host side of this library (io.c / model.c, the
+ * replacements of emberllm's src/io.c and src/model.c) calls to run the token
+ * loop on the device. Every function returns 0 on success or a nonzero status,
+ * with a message available from ember_cuda_error(); the host converts failures
+ * into ember_die("cuda: ...") to keep emberllm's fatal-error convention.
+ *
+ * Only plain C types cross this boundary: host pointers, sizes, opaque handles.
+ */
+#ifndef EMBER_B200_CUDA_H
+#define EMBER_B200_CUDA_H
+
+#include <stdint.h>
+#include "ember.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct EmberCudaModel EmberCudaModel;
+typedef struct EmberCudaState EmberCudaState;
+
+/* One 2-D weight as it sits in the host mapping. */
+typedef struct {
+    const void *data;   /* host pointer into the .ember mapping                     */
+    int32_t dtype;      /* EMBER_DT_F32 / Q8_0 / Q4_0                                */
+    int32_t rows;       /* output rows (d_out)                                       */
+    int32_t cols;       /* input length (n_in)                                       */
+} EmberCudaMat;
+
+/* Everything the device needs from a model, resolved by the host (the same
+ * tensors emberllm's ember_state_new_ex resolves, ref src/model.c:144-159).
+ * Per-layer arrays have n_layers entries; optional vectors are NULL. */
+typedef struct {
+    int32_t dim, hidden, n_layers, n_heads, n_kv_heads, head_dim, vocab;
+    float   norm_eps;
+    int32_t qk_norm;
+    int32_t rope_neox;                   /* 1: NEOX half-split pairs, 0: interleaved */
+    EmberCudaMat tok_emb, lm_head;       /* lm_head.data == tok_emb.data when tied */
+    const float *final_norm;
+    const EmberCudaMat *wq, *wk, *wv, *wo, *w1, *w2, *w3;
+    const float *const *attn_norm, *const *ffn_norm;
+    const float *const *q_norm, *const *k_norm;   /* used when qk_norm != 0      */
+    const float *const *b_q, *const *b_k, *const *b_v;
+} EmberCudaModelDesc;
+
+/* Parameters of the device expf. The device computes exp(x) with a fixed
+ * double-precision recipe (range reduction by ln2 in two parts + a degree-12
+ * Taylor polynomial, all constants supplied by the host so host and device use
+ * identical bits) and rounds to float. The host scans every float input in
+ * [lo, hi] once against the C library's expf and lists, in an open-addressing
+ * table, the inputs where the library's result differs; the device consults the
+ * table only when its double result lies within `delta` float-ulps of a rounding
+ * midpoint (every listed input satisfies this by construction) or the result is
+ * not a normal float. Below lo the result is +0, above hi it is +inf. */
+typedef struct {
+    double coef[13];        /* polynomial coefficients, coef[k] ~ 1/k!                */
+    double inv_ln2, ln2_hi, ln2_lo, shifter;
+    double delta;           /* midpoint window, in float ulps                         */
+    float  lo, hi;          /* scanned input range                                    */
+    uint32_t n_slots;       /* power of two                                           */
+    uint32_t n_entries;
+    const uint32_t *slots;  /* 2*n_slots words: (x bits, expf bits); empty key = ~0u */
+} EmberExpfParams;
+
+/* The double-precision exp recipe shared by host and device (see above). */
+#define EMBER_EXPF_EMPTY 0xFFFFFFFFu
+
+/* ---- device + model ---- */
+/* Uploads (and repacks) the weights to the current device. `expf_params` is
+ * copied. The device is EMBER_CUDA_DEVICE (default 0). */
+int  ember_cuda_model_upload(const EmberCudaModelDesc *desc, const EmberExpfParams *expf_params,
+                             EmberCudaModel **out);
+void ember_cuda_model_free(EmberCudaModel *m);
+/* bytes of weights the device holds for this model (after repacking) */
+uint64_t ember_cuda_model_bytes(const EmberCudaModel *m);
+
+/* ---- state ---- */
+/* rope_cs: host table [ctx][head_dim/2][2] of (cos, sin), computed by the host
+ * with the reference's own float expressions (ref src/model.c:69-71). */
+int  ember_cuda_state_new(EmberCudaModel *m, int ctx, int kv_fp16, const float *rope_cs,
+                          EmberCudaState **out);
+void ember_cuda_state_free(EmberCudaState *s);
+
+/* one decode step; copies vocab logits to host_logits (pinned or pageable) */
+int  ember_cuda_forward(EmberCudaState *s, int tok, int pos, float *host_logits);
+/* n tokens at start..start+n-1; last token's logits to host_logits */
+int  ember_cuda_prefill(EmberCudaState *s, const int *ids, int n, int start, float *host_logits);
+/* n_steps greedy steps without host round trips: step i feeds token t_i at pos+i
+ * (t_0 = tok) and t_{i+1} = first argmax of its logits; writes t_1..t_n to
+ * host_tokens and the last step's logits to host_logits (if not NULL). */
+int  ember_cuda_greedy(EmberCudaState *s, int tok, int pos, int n_steps, int *host_tokens,
+                       float *host_logits);
+
+/* the state's pinned host logits buffer (vocab floats), owned by the state */
+float       *ember_cuda_state_host_logits(EmberCudaState *s);
+
+/* introspection for tests and benchmarks */
+void        *ember_cuda_state_stream(EmberCudaState *s);      /* cudaStream_t */
+const float *ember_cuda_state_logits_dev(EmberCudaState *s);  /* device pointer */
+int          ember_cuda_state_launches_per_step(const EmberCudaState *s);
+const char  *ember_cuda_error(void);
+/* 1 if this library was built with sm_100a device code and a device is usable */
+int          ember_cuda_available(void);
+
+/* ---- host helpers implemented in C (glibc-dependent tables) ---- */
+/* Builds (or loads from the cache directory $EMBER_CACHE_DIR, default
+ * ~/.cache/ember_b200) the expf exception table for THIS host's C library.
+ * The returned params point at static storage valid for the process. */
+int  ember_host_expf_params(EmberExpfParams *out);
+/* the device recipe evaluated on the host (identical bits); for tests */
+float ember_host_expf_emulated(const EmberExpfParams *p, float x);
+/* fills [ctx][hd/2][2] with the reference's cos/sin values */
+void ember_host_rope_table(float *out, int ctx, int head_dim, float theta);
+
+/* ---- extension on the public API (host C) ---- */
+/* Greedy decoding on the device: equivalent to n iterations of
+ *   logits = ember_forward(m, s, tok, pos + i); tok = first argmax(logits);
+ * writing each chosen token to out_tokens[i]. The state's logits hold the last
+ * step's logits afterwards. Returns s's logits. */
+float *ember_forward_greedy(EmberModel *m, EmberState *s, int tok, int pos, int n,
+                            int *out_tokens);
+/* the device-side state behind a public state (for timing hooks) */
+EmberCudaState *ember_state_cuda(EmberState *s);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* EMBER_B200_CUDA_H */
