@@ -1,0 +1,407 @@
+#!/usr/bin/env python3
+"""Benchmark of the emberllm token loop on B200 (decode tok/s + HBM GB/s).
+
+Workload (the config the headline metric is quoted on):
+Qwen3-0.6B-shape decoder, Q8_0, synthetic N(0, 0.02) weights (seed 0), KV cache
+prefilled with `--depth` (128) uniform random tokens (seed 1), then single-stream
+greedy decode of `--tokens` (128) tokens. One STEP = those 128 greedy tokens from
+position `depth` (the cache is rewound to `depth` for every step).
+
+  value  device-resident decode: the step is ember_forward_greedy (captured CUDA
+         graphs, argmax on the device, no host round trip per token), timed with
+         CUDA events on the state's stream; tok/s over all ranks.
+  e2e    the same tokens through the public C API the reference's callers use:
+         ember_forward per token (host->device token/position from pinned memory,
+         device->host copy of all vocab logits into pinned memory), host argmax.
+  roofline  the kernel kind with the largest share of a decode step, timed live
+         (every layer in turn, outside the graph) against its algorithmic bytes.
+  cpu_baseline  the reference's own `ember bench` (shipped -O3 -ffast-math flags)
+         on this host's cores, best thread count of a sweep, bounded sample.
+
+Multi-GPU: `torchrun --nproc-per-node N bench.py --gpus N`: one independent
+replica per GPU, no collective on the data path (weak scaling); the step time is
+the max over ranks.
+
+`--impl reference` times the reference's CPU implementation (oracle/_ref, built
+from its own sources) on the same workload, rank 0 only.
+"""
+import argparse
+import ctypes
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+KIND_NAMES = ["qkv_gemv", "attention", "wo_gemv", "w13_swiglu_gemv", "w2_gemv", "lm_head_gemv"]
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--config", default="qwen3-0.6b")
+    p.add_argument("--depth", type=int, default=128)
+    p.add_argument("--tokens", type=int, default=128)
+    p.add_argument("--e2e-steps", type=int, default=2)
+    p.add_argument("--cpu-baseline", type=int, default=1)
+    return p.parse_args()
+
+
+# ------------------------------------------------------------------ helpers ---
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def ncu_traffic(kind_name, config):
+    """per-launch DRAM bytes from the committed ncu summary (profiles/), or None"""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.txt")
+    try:
+        for line in open(path):
+            parts = line.split()
+            if len(parts) >= 3 and parts[0] == kind_name and parts[1] == config:
+                return float(parts[2])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled during the timed region"""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reference_binary():
+    """the reference CLI built by oracle/Makefile; AVX-512 build where the CPU has it"""
+    flags = ""
+    try:
+        flags = open("/proc/cpuinfo").read()
+    except OSError:
+        pass
+    v4 = os.path.join(ROOT, "oracle", "_ref", "ember_ref_v4")
+    v3 = os.path.join(ROOT, "oracle", "_ref", "ember_ref_v3")
+    if " avx512f " in flags and " avx512bw " in flags and os.path.exists(v4):
+        return v4
+    return v3 if os.path.exists(v3) else None
+
+
+def ref_cli_bench(binary, model, pp, tg, threads, reps=1):
+    out = subprocess.run([binary, "bench", model, "--pp", str(pp), "--tg", str(tg), "--threads",
+                          str(threads), "--reps", str(reps)], capture_output=True, text=True,
+                         timeout=600)
+    m = re.search(r"decode\s+\(tg\d+\):\s+([\d.]+)\s+tok/s", out.stdout)
+    if out.returncode != 0 or not m:
+        raise RuntimeError("reference bench failed: " + out.stdout[-300:] + out.stderr[-300:])
+    pm = re.search(r"prefill \(pp\d+\):\s+([\d.]+)\s+tok/s", out.stdout)
+    return float(m.group(1)), float(pm.group(1)) if pm else None
+
+
+def thread_sweep():
+    n = os.cpu_count() or 1
+    return sorted(c for c in {1, 4, 8, n // 2, n} if 1 <= c <= n)
+
+
+def cpu_baseline(model, depth, budget_tg=16):
+    """reference `ember bench` at depth `depth`, best decode over a thread sweep"""
+    binary = reference_binary()
+    if not binary:
+        return None
+    best = (0.0, 1, None)
+    for t in thread_sweep():
+        try:
+            tg, pp = ref_cli_bench(binary, model, depth, budget_tg, t)
+        except (RuntimeError, subprocess.TimeoutExpired):
+            continue
+        if tg > best[0]:
+            best = (tg, t, pp)
+    if best[0] == 0.0:
+        return None
+    return {"value": round(best[0], 2), "unit": "tok/s", "cores": best[1], "kind": "reference",
+            "prefill_tok_s": best[2],
+            "sample": "reference `ember bench --pp %d --tg %d --reps 1` (%s, shipped -O3 "
+                      "-ffast-math flags), decode tok/s at depth %d, best of threads %s on %d "
+                      "host cores" % (depth, budget_tg, os.path.basename(binary), depth,
+                                      thread_sweep(), os.cpu_count() or 1)}
+
+
+# ------------------------------------------------------------------ ranks -----
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        os.environ["EMBER_CUDA_DEVICE"] = str(local)
+        import torch
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+        return world, rank, local, dist
+    return 1, 0, 0, None
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def max_over_ranks(dist, value):
+    if dist is None:
+        return value
+    import torch
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ arms ------
+
+def run_ours(args, world, rank, local, dist):
+    import numpy as np
+    from emberllm_b200 import Ember, load, synth
+
+    cfg = synth.CONFIGS[args.config]
+    if rank == 0:
+        path = synth.ensure_model(args.config)
+    barrier(dist)
+    path = synth.ensure_model(args.config)
+    lib = load()
+    for name, res, argt in [
+            ("ember_cuda_mark", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+            ("ember_cuda_elapsed_ms", ctypes.c_int,
+             [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float)]),
+            ("ember_cuda_time_kernel", ctypes.c_int,
+             [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float),
+              ctypes.POINTER(ctypes.c_double)])]:
+        getattr(lib, name).restype = res
+        getattr(lib, name).argtypes = argt
+
+    depth, ntok = args.depth, args.tokens
+    e = Ember(path, ctx=depth + ntok + 8)
+    cs = lib.ember_state_cuda(e.st)
+    rng = np.random.default_rng(1)
+    prompt = [int(t) for t in rng.integers(0, e.vocab, depth)]
+
+    def elapsed(a, b):
+        ms = ctypes.c_float()
+        assert lib.ember_cuda_elapsed_ms(cs, a, b, ctypes.byref(ms)) == 0, lib.ember_cuda_error()
+        return ms.value / 1e3
+
+    # prefill (the reference's pp) -- timed once
+    e.prefill(prompt)
+    lib.ember_cuda_mark(cs, 4)
+    e.prefill(prompt)
+    lib.ember_cuda_mark(cs, 5)
+    prefill_s = elapsed(4, 5)
+    first = int(np.argmax(np.ctypeslib.as_array(e.forward(prompt[-1], depth - 1), (e.vocab,))))
+
+    for _ in range(args.warmup):
+        e.greedy(first, depth, ntok)
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier(dist)
+    lib.ember_cuda_mark(cs, 0)
+    for _ in range(args.steps):
+        e.greedy(first, depth, ntok)
+    lib.ember_cuda_mark(cs, 1)
+    t = elapsed(0, 1)
+    clk = clocks.stop()
+    t_max = max_over_ranks(dist, t)
+
+    # end to end through the public API: ember_forward per token, host argmax
+    barrier(dist)
+    lib.ember_cuda_mark(cs, 2)
+    for _ in range(args.e2e_steps):
+        tok = first
+        for i in range(ntok):
+            logits = np.ctypeslib.as_array(e.forward(tok, depth + i), (e.vocab,))
+            tok = int(np.argmax(logits))
+    lib.ember_cuda_mark(cs, 3)
+    t_e2e = max_over_ranks(dist, elapsed(2, 3))
+
+    # roofline of the dominant kernel kind, timed live (overwrites the state)
+    kinds = []
+    L = cfg["n_layers"]
+    for kind in range(6):
+        ms, by = ctypes.c_float(), ctypes.c_double()
+        assert lib.ember_cuda_time_kernel(cs, kind, 5, ctypes.byref(ms), ctypes.byref(by)) == 0, \
+            lib.ember_cuda_error()
+        per_step = ms.value * (1 if kind == 5 else L)
+        kinds.append((per_step, kind, ms.value, by.value))
+    kinds.sort(reverse=True)
+    _, dk, dms, dbytes = kinds[0]
+    peak, peak_kind = measured_peaks()
+    achieved = dbytes / (dms / 1e3) / 1e9
+    launches = 1 + 5 * L + 1 + 1     # embed, 5 per layer, lm_head, argmax
+    e.close()
+
+    total_tokens = world * args.steps * ntok
+    value = total_tokens / t_max
+    ms_per_step = t_max / args.steps * 1e3
+    step_bytes = synth.weight_bytes_per_token(cfg)
+    kvd = cfg["n_kv_heads"] * cfg["head_dim"]
+    avg_pos = depth + (ntok - 1) / 2.0
+    kv_bytes = 2 * cfg["n_layers"] * kvd * 4 * (avg_pos + 1) + 2 * cfg["n_layers"] * kvd * 4
+    line = {
+        "metric": "decode tok/s (Qwen3-0.6B Q8_0, 1 GPU); HBM GB/s; prefill tok/s",
+        "value": round(value, 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int8 dot / fp32 (Q8_0 weights, exact reference arithmetic)",
+        "data": "synthetic: N(0,0.02) weights seed 0, uniform random prompt seed 1",
+        "config": {"workload": "%s Q8_0 single-stream greedy decode of %d tokens at depth %d"
+                               % (args.config, ntok, depth),
+                   "model": args.config, "depth": depth, "tokens_per_step": ntok,
+                   "kv_cache": "fp32", "parallelism": "replicas, one per GPU" if world > 1 else "1 GPU",
+                   "l2": "weights 634 MB per token > 126 MB L2 (no flush needed)"},
+        "hbm_gbs_step": round((step_bytes + kv_bytes) * value / world / 1e9, 1),
+        "bytes_per_token": int(step_bytes + kv_bytes),
+        "prefill_tok_s": round(depth / prefill_s, 1),
+        "prefill_note": "prefill runs as sequential exact decode steps (ember_prefill)",
+        "e2e": {"value": round(world * args.e2e_steps * ntok / t_e2e, 2), "unit": "tok/s",
+                "h2d_bytes_per_step": ntok * 8, "d2h_bytes_per_step": ntok * (cfg["vocab_size"] * 4 + 4),
+                "path": "ember_forward per token (pinned host logits) + host argmax"},
+        "gpu_launches": args.steps * ntok * launches,
+        "roofline": {"kernel": KIND_NAMES[dk], "bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4),
+                     "traffic": ncu_traffic(KIND_NAMES[dk], args.config),
+                     "bytes_per_launch": int(dbytes), "us_per_launch": round(dms * 1e3, 3)},
+        "kernel_shares": {KIND_NAMES[k]: round(ps, 4) for ps, k, _, _ in kinds},
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and args.cpu_baseline:
+        cb = cpu_baseline(path, depth)
+        line["cpu_baseline"] = cb
+    return line
+
+
+def run_reference(args, world, rank):
+    """the reference's own CPU implementation on this host (oracle/_ref)"""
+    if rank != 0:
+        return None
+    from emberllm_b200 import synth
+    binary = reference_binary()
+    if not binary:
+        return {"impl": "reference", "unavailable": "oracle/_ref was not built on this machine"}
+    path = synth.ensure_model(args.config)
+    depth, tg = args.depth, 16
+    sweep = {}
+    for t in thread_sweep():
+        try:
+            sweep[t] = ref_cli_bench(binary, path, depth, tg, t)[0]
+        except (RuntimeError, subprocess.TimeoutExpired):
+            pass
+    best_t = max(sweep, key=sweep.get)
+    for _ in range(max(0, args.warmup - 1)):
+        ref_cli_bench(binary, path, depth, tg, best_t)
+    vals = [ref_cli_bench(binary, path, depth, tg, best_t)[0] for _ in range(args.steps)]
+    v = statistics.mean(vals)
+    return {
+        "impl": "reference",
+        "metric": "decode tok/s (Qwen3-0.6B Q8_0, 1 GPU); HBM GB/s; prefill tok/s",
+        "value": round(v, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(tg / v * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot / fp32 (Q8_0)",
+        "data": "synthetic: N(0,0.02) weights seed 0",
+        "config": {"workload": "%s Q8_0 decode at depth %d (reference CPU, %d tokens per step)"
+                               % (args.config, depth, tg), "model": args.config},
+        "cpu_baseline": {"value": round(v, 2), "unit": "tok/s", "cores": best_t, "kind": "reference",
+                         "sample": "reference `ember bench --pp %d --tg %d --reps 1` per step, "
+                                   "%s, threads %d (best of %s)"
+                                   % (depth, tg, os.path.basename(binary), best_t, sweep)},
+        "e2e": {"value": round(v, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        # CPU only: rank 0 runs, the other ranks exit without work
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        line = run_reference(args, world, rank)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    world, rank, local, dist = dist_setup(args)
+    try:
+        line = run_ours(args, world, rank, local, dist)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

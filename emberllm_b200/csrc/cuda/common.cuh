@@ -63,24 +63,125 @@ EMB_DEV int8_t quant_lane(float x, float *dq) {
     return (int8_t)(int)q;
 }
 
-// Bytes of one quantized row: Q8_0 32 int8 per block, Q4_0 16 bytes per block.
+// Bytes of one row in the device layout: Q8_0 32 int8 per block, Q4_0 16 bytes
+// per block, fp32 4 bytes per element.
 __host__ __device__ inline size_t qrow_bytes(int dtype, int cols) {
     return dtype == EMBER_DT_Q4_0 ? (size_t)cols / 2 : (dtype == EMBER_DT_Q8_0 ? (size_t)cols : (size_t)cols * 4);
 }
 
 // ---- programmatic dependent launch (PDL) -----------------------------------
 // Every kernel of the token step is launched with programmatic stream
-// serialization: it lets the NEXT kernel start as soon as all of its CTAs have
-// begun (launch_dependents), and waits for the PREVIOUS kernel to finish and
-// flush its memory (wait) before touching anything that kernel wrote. The span
-// between the two is used to prefetch this kernel's weights into L2.
+// serialization and begins with
+//
+//     [pre-wait work]  griddepcontrol.wait  griddepcontrol.launch_dependents ...
+//
+// The wait returns when the previous kernel (N-1) has finished and flushed its
+// memory; only then does this kernel (N) allow the next one (N+1) to launch.
+// Consequently, when kernel N+1 starts its pre-wait work, every CTA of kernel N
+// has passed its wait, so kernel N-1 and everything before it is complete: the
+// pre-wait work of a kernel may read weights, tables, and anything written two
+// or more launches earlier (the KV cache of previous positions, the step's
+// position word), and must not read what its immediate predecessor writes.
 EMB_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 EMB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+EMB_DEV void pdl_wait_then_release() {
+    pdl_wait();
+    pdl_launch_dependents();
+}
+
+// ---- exact sequential sums ---------------------------------------------------
+// sum = ((0 + v[0]) + v[1]) + ... in index order: the reference's loop. The
+// additions form one dependent chain; the loads are batched into registers
+// ahead of it so the chain runs at the adder's latency.
+EMB_DEV float chain_sum(float s, const float *v, int n) {
+    int i = 0;
+    for (; i + 16 <= n; i += 16) {
+        float r[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) r[j] = v[i + j];
+#pragma unroll
+        for (int j = 0; j < 16; j++) s = __fadd_rn(s, r[j]);
+    }
+    for (; i < n; i++) s = __fadd_rn(s, v[i]);
+    return s;
+}
+
+// sum of v[i]*v[i] in index order (products rounded, then added)
+EMB_DEV float chain_sumsq(const float *v, int n) {
+    float s = 0.0f;
+    int i = 0;
+    for (; i + 16 <= n; i += 16) {
+        float r[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) r[j] = v[i + j];
+#pragma unroll
+        for (int j = 0; j < 16; j++) s = __fadd_rn(s, __fmul_rn(r[j], r[j]));
+    }
+    for (; i < n; i++) s = __fadd_rn(s, __fmul_rn(v[i], v[i]));
+    return s;
+}
+
+// ---- bulk async copies (TMA, non-tensor form) and mbarriers ----------------
+EMB_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+EMB_DEV void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// make mbarrier initialisation visible to the async (TMA) proxy
+EMB_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+EMB_DEV void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// global -> shared bulk copy completing on `bar`; dst, src 16-byte aligned,
+// bytes a multiple of 16. No multicast.
+EMB_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+EMB_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: each try_wait blocks for a hardware-chosen slice; after
+// MBAR_TRIES slices (seconds in total) the wait gives up, records `code` in the
+// device error word and returns false, so a lost copy can never hang the GPU.
+constexpr uint32_t MBAR_TRIES = 1u << 22;
+EMB_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+    for (uint32_t i = 0; i < MBAR_TRIES; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    if (err) atomicExch(err, code);
+    return false;
+}
+
+// CTA-wide wait: one thread waits on the mbarrier (acquiring the copied bytes),
+// then a CTA barrier releases the others, who see the bytes through it.
+EMB_DEV void mbar_wait_cta(uint64_t *bar, uint32_t parity, int *err, int code) {
+    if (threadIdx.x == 0) mbar_wait(bar, parity, err, code);
+    __syncthreads();
+}
 
 // Bulk L2 prefetch of [p, p+bytes); p 16-byte aligned, bytes a multiple of 16.
 EMB_DEV void prefetch_l2(const void *p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
+
+// device error codes (written to the state's error word, read by the host)
+enum { ERR_NONE = 0, ERR_GEMV_WAIT = 1, ERR_ATTN_WAIT = 2 };
 
 // The device expf: the host C library's expf, reproduced from the recipe and
 // exception table described in expf_core.h.

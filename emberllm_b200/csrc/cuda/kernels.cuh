@@ -13,6 +13,14 @@
 // and the step ends with gemv<IN_NORM, EPI_STORE> over lm_head (final norm
 // fused) plus, for device-side greedy decoding, an argmax.
 //
+// Data movement. Weight tiles (R consecutive rows: their quant bytes and their
+// fp16 scales, each a contiguous range in the device layout) are moved into
+// shared memory by bulk asynchronous copies (TMA, cp.async.bulk) that complete
+// on an mbarrier. The copies of a CTA's first tiles are issued BEFORE the
+// programmatic-launch wait, so they overlap the previous kernel; later tiles
+// stream through a ring of stages. Attention stages each chunk of the cache the
+// same way. Every wait on an mbarrier is bounded (common.cuh).
+//
 // Every fp32 result is bit-identical to emberllm's deterministic build: see the
 // order notes at each step and the rules in common.cuh.
 #pragma once
@@ -22,16 +30,17 @@
 namespace emb {
 
 constexpr int GEMV_THREADS = 256;
-constexpr int GEMV_ROWS = 32;   // output rows per tile = one Q8 block of outputs
+constexpr int GEMV_MAX_ROWS = 32;     // rows per tile (SwiGLU: exactly one Q8 block of h)
+constexpr int GEMV_MAX_STAGES = 4;
 constexpr int ATTN_THREADS = 256;
 
 enum { IN_RAW = 0, IN_NORM = 1, IN_QUANT = 2 };
 enum { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2 };
 
 // ctl words in device memory, read by the step's kernels (so one captured graph
-// serves every position): [0] pos, [1] token, [2] number of greedy tokens
-// written, [3] position of ids[0] during a prefill.
-enum { CTL_POS = 0, CTL_TOK = 1, CTL_NOUT = 2, CTL_BASE = 3, CTL_WORDS = 4 };
+// serves every position): pos, token, number of greedy tokens written, position
+// of ids[0] during a prefill, and the device error word.
+enum { CTL_POS = 0, CTL_TOK = 1, CTL_NOUT = 2, CTL_BASE = 3, CTL_ERR = 4, CTL_WORDS = 8 };
 
 // A weight matrix in the device layout: rows of quantized bytes (Q8_0: 32 int8
 // per block; Q4_0: 16 bytes per block, nibble order as in the file) and, apart,
@@ -47,8 +56,11 @@ struct GemvSeg {
 struct GemvArgs {
     GemvSeg seg[3];
     int nseg, cols;
+    int rows;                 // rows per tile R (<= 32; SwiGLU: 32)
     int tiles[4];             // tiles[k] = first tile of segment k; tiles[nseg] = total
-    int prefetch_tiles;       // tiles of its own each CTA prefetches into L2 before waiting
+    int stages;               // shared-memory ring depth (quantized weights)
+    int stage_bytes;          // bytes of one stage (all sub-tiles)
+    int quantized;            // 1: Q8_0/Q4_0 segments (bulk copies); 0: fp32 segments
     // input
     const float *x;           // IN_RAW / IN_NORM: fp32 input
     const float *norm_w;      // IN_NORM
@@ -58,26 +70,33 @@ struct GemvArgs {
     const float *xf;          // IN_QUANT: fp32 copy for fp32 weights (may be NULL)
     int8_t *xq_out;           // IN_RAW: CTA 0 also writes the quantized input (op tests)
     float *xd_out;
-    // EPI_SWIGLU outputs: quantized h, its scales, fp32 h
+    // EPI_SWIGLU outputs: quantized h, its scales, fp32 h (fp32 only when needed)
     int8_t *hq;
     float *hd;
     float *hf;
+    int *err;
     ExpfDev ex;
 };
 
 __host__ __device__ inline int gemv_p_stride(int nb) { return nb | 1; }
+__host__ __device__ inline size_t pad16(size_t n) { return (n + 15) / 16 * 16; }
+
+// bytes of one sub-tile (R rows of one matrix) inside a stage
+__host__ __device__ inline size_t gemv_sub_bytes(int dtype, int rows, int cols) {
+    return pad16((size_t)rows * qrow_bytes(dtype, cols)) + pad16((size_t)rows * (cols / 32) * 2);
+}
 
 // dynamic shared memory of gemv_kernel
-__host__ inline size_t gemv_smem_bytes(int cols, bool need_xf) {
-    int nb = cols / 32;
-    size_t b = ((size_t)cols + 15) / 16 * 16;                  // xq
-    b += (size_t)(nb > 0 ? nb : 1) * 4;                         // xd
-    b = (b + 15) / 16 * 16;
+__host__ inline size_t gemv_smem_bytes(const GemvArgs &a, bool need_xf) {
+    const int cols = a.cols, nb = cols / 32;
+    size_t b = a.quantized ? (size_t)a.stages * a.stage_bytes : 0;
+    b += pad16(cols);                                           // xq
+    b += pad16((size_t)(nb > 0 ? nb : 1) * 4);                  // xd
     if (need_xf) b += (size_t)cols * 4;                         // xf
-    size_t p = (size_t)2 * GEMV_ROWS * gemv_p_stride(nb) * 4;   // P (also sq scratch)
+    size_t p = (size_t)2 * GEMV_MAX_ROWS * gemv_p_stride(nb) * 4;
     size_t sq = (size_t)cols * 4;
-    b += p > sq ? p : sq;
-    b += 2 * GEMV_ROWS * 4;                                     // row sums
+    b += p > sq ? p : sq;                                       // P (also sq scratch)
+    b += 2 * GEMV_MAX_ROWS * 4;                                 // row sums
     return b;
 }
 
@@ -85,17 +104,17 @@ EMB_DEV GemvSeg pick_seg(const GemvArgs &a, int k) {
     return k == 0 ? a.seg[0] : (k == 1 ? a.seg[1] : a.seg[2]);
 }
 
-// int8 dot of one Q8_0 weight block (32 B) with one activation block
+// int8 dot of one Q8_0 weight block (32 B) with one activation block, both in smem
 EMB_DEV int dot_q8_block(const uint8_t *w, const int8_t *xq) {
-    uint4 w0 = __ldg(reinterpret_cast<const uint4 *>(w));
-    uint4 w1 = __ldg(reinterpret_cast<const uint4 *>(w) + 1);
+    int4 w0 = reinterpret_cast<const int4 *>(w)[0];
+    int4 w1 = reinterpret_cast<const int4 *>(w)[1];
     int4 a0 = reinterpret_cast<const int4 *>(xq)[0];
     int4 a1 = reinterpret_cast<const int4 *>(xq)[1];
     int acc = 0;
-    acc = __dp4a((int)w0.x, a0.x, acc); acc = __dp4a((int)w0.y, a0.y, acc);
-    acc = __dp4a((int)w0.z, a0.z, acc); acc = __dp4a((int)w0.w, a0.w, acc);
-    acc = __dp4a((int)w1.x, a1.x, acc); acc = __dp4a((int)w1.y, a1.y, acc);
-    acc = __dp4a((int)w1.z, a1.z, acc); acc = __dp4a((int)w1.w, a1.w, acc);
+    acc = __dp4a(w0.x, a0.x, acc); acc = __dp4a(w0.y, a0.y, acc);
+    acc = __dp4a(w0.z, a0.z, acc); acc = __dp4a(w0.w, a0.w, acc);
+    acc = __dp4a(w1.x, a1.x, acc); acc = __dp4a(w1.y, a1.y, acc);
+    acc = __dp4a(w1.z, a1.z, acc); acc = __dp4a(w1.w, a1.w, acc);
     return acc;
 }
 
@@ -103,7 +122,7 @@ EMB_DEV int dot_q8_block(const uint8_t *w, const int8_t *xq) {
 // (byte i >> 4) - 8 (ref src/kernels.c:175-179). Unsigned nibbles fit in a
 // signed byte, so sum((n-8)*a) = sum(n*a) - 8*sum(a), all exact in int32.
 EMB_DEV int dot_q4_block(const uint8_t *w, const int8_t *xq) {
-    uint4 v = __ldg(reinterpret_cast<const uint4 *>(w));
+    uint4 v = reinterpret_cast<const uint4 *>(w)[0];
     int4 a0 = reinterpret_cast<const int4 *>(xq)[0];
     int4 a1 = reinterpret_cast<const int4 *>(xq)[1];
     const uint32_t m = 0x0F0F0F0Fu;
@@ -120,57 +139,93 @@ EMB_DEV int dot_q4_block(const uint8_t *w, const int8_t *xq) {
     return acc - 8 * sa;
 }
 
-// Issue L2 prefetches for one tile of a segment (weights are read-only, so this
-// is safe before the dependency wait).
-EMB_DEV void prefetch_tile(const GemvSeg &g, int row0, int cols) {
-    int nrows = min(GEMV_ROWS, g.rows - row0);
-    if (nrows <= 0 || g.dtype == EMBER_DT_F32) return;
-    size_t rb = qrow_bytes(g.dtype, cols);
-    uint32_t qbytes = (uint32_t)(rb * (size_t)nrows) & ~15u;
-    if (qbytes) prefetch_l2(g.q + rb * (size_t)row0, qbytes);
-    int nb = cols / 32;
-    uint32_t sbytes = (uint32_t)((size_t)nrows * nb * 2) & ~15u;
-    if (sbytes) prefetch_l2(g.s + (size_t)row0 * nb, sbytes);
+// Which segment / first row / row count a tile covers, for sub-tile `sub`.
+struct TileRef {
+    GemvSeg g;
+    int row0, nrows;
+};
+
+template <int EPI>
+EMB_DEV TileRef tile_ref(const GemvArgs &a, int t, int sub) {
+    TileRef r;
+    int k = 0;
+    if (EPI == EPI_SWIGLU) {
+        k = sub;
+        r.row0 = t * a.rows;
+    } else {
+        while (k + 1 < a.nseg && t >= a.tiles[k + 1]) k++;
+        r.row0 = (t - a.tiles[k]) * a.rows;
+    }
+    r.g = pick_seg(a, k);
+    r.nrows = min(a.rows, r.g.rows - r.row0);
+    return r;
+}
+
+// Thread 0: bulk-copy tile t (all its sub-tiles) into stage buffer `dst`.
+template <int EPI>
+EMB_DEV void issue_tile(const GemvArgs &a, int t, unsigned char *dst, uint64_t *bar) {
+    constexpr int nsub = EPI == EPI_SWIGLU ? 2 : 1;
+    const int nb = a.cols / 32;
+    uint32_t total = 0;
+    TileRef tr[nsub];
+#pragma unroll
+    for (int sub = 0; sub < nsub; sub++) {
+        tr[sub] = tile_ref<EPI>(a, t, sub);
+        total += (uint32_t)(tr[sub].nrows * qrow_bytes(tr[sub].g.dtype, a.cols));
+        total += (uint32_t)pad16((size_t)tr[sub].nrows * nb * 2);
+    }
+    mbar_expect_tx(bar, total);
+    size_t off = 0;
+#pragma unroll
+    for (int sub = 0; sub < nsub; sub++) {
+        const GemvSeg &g = tr[sub].g;
+        const size_t rb = qrow_bytes(g.dtype, a.cols);
+        const uint32_t qb = (uint32_t)(tr[sub].nrows * rb);
+        const uint32_t sb = (uint32_t)pad16((size_t)tr[sub].nrows * nb * 2);
+        bulk_g2s(dst + off, g.q + rb * (size_t)tr[sub].row0, qb, bar);
+        // scale rows are padded on the device by 16 bytes, so rounding up is in bounds
+        bulk_g2s(dst + off + pad16((size_t)a.rows * rb), g.s + (size_t)tr[sub].row0 * nb, sb, bar);
+        off += gemv_sub_bytes(g.dtype, a.rows, a.cols);
+    }
 }
 
 template <int IN, int EPI>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    const int tid = threadIdx.x;
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(8) uint64_t bars[GEMV_MAX_STAGES];
+    __shared__ float s_scale;
+    constexpr int nsub = EPI == EPI_SWIGLU ? 2 : 1;
+    const int tid = threadIdx.x, R = a.rows;
     const int cols = a.cols, nb = cols / 32, pstride = gemv_p_stride(nb);
     const int total = a.tiles[a.nseg];
-    const int ntiles_seg = EPI == EPI_SWIGLU ? total : 0;  // swiglu: tile t covers seg0 and seg1
+    const int my_tiles = (int)blockIdx.x < total ? (total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const bool need_xf = IN != IN_QUANT || !a.quantized;
+    const int S = a.quantized ? a.stages : 0;
 
-    bool has_f32 = false;
-    for (int k = 0; k < (EPI == EPI_SWIGLU ? 2 : a.nseg); k++) has_f32 |= pick_seg(a, k).dtype == EMBER_DT_F32;
-    const bool need_xf = IN != IN_QUANT || has_f32;
-
-    int8_t *xq_s = reinterpret_cast<int8_t *>(smem);
-    size_t off = ((size_t)cols + 15) / 16 * 16;
+    unsigned char *stage0 = smem;
+    size_t off = (size_t)S * a.stage_bytes;
+    int8_t *xq_s = reinterpret_cast<int8_t *>(smem + off);
+    off += pad16(cols);
     float *xd_s = reinterpret_cast<float *>(smem + off);
-    off = (off + (size_t)(nb > 0 ? nb : 1) * 4 + 15) / 16 * 16;
+    off += pad16((size_t)(nb > 0 ? nb : 1) * 4);
     float *xf_s = reinterpret_cast<float *>(smem + off);
     if (need_xf) off += (size_t)cols * 4;
     float *P = reinterpret_cast<float *>(smem + off);
-    size_t psz = (size_t)2 * GEMV_ROWS * pstride * 4, sqsz = (size_t)cols * 4;
+    size_t psz = (size_t)2 * GEMV_MAX_ROWS * pstride * 4, sqsz = (size_t)cols * 4;
     off += psz > sqsz ? psz : sqsz;
     float *rowsum = reinterpret_cast<float *>(smem + off);
-    __shared__ float s_scale;
 
-    pdl_launch_dependents();
-    if (tid == 0) {
-        int k = 0;
-        for (int t = blockIdx.x, n = 0; t < total && n < a.prefetch_tiles; t += gridDim.x, n++) {
-            if (EPI == EPI_SWIGLU) {
-                prefetch_tile(a.seg[0], t * GEMV_ROWS, cols);
-                prefetch_tile(a.seg[1], t * GEMV_ROWS, cols);
-            } else {
-                while (k + 1 < a.nseg && t >= a.tiles[k + 1]) k++;
-                prefetch_tile(pick_seg(a, k), (t - a.tiles[k]) * GEMV_ROWS, cols);
-            }
-        }
+    // ---- pre-wait: only weights (the tiles and the norm vector) ----
+    if (S > 0 && tid == 0) {
+        for (int s = 0; s < S; s++) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+        for (int k = 0; k < S && k < my_tiles; k++)
+            issue_tile<EPI>(a, blockIdx.x + k * gridDim.x, stage0 + (size_t)k * a.stage_bytes, &bars[k]);
     }
-    pdl_wait();
+    float *nw_s = P;   // the norm weights live in P until the tiles need it
+    if (IN == IN_NORM)
+        for (int i = tid; i < cols; i += GEMV_THREADS) nw_s[i] = a.norm_w[i];
+    pdl_wait_then_release();
 
     // ---- prologue: the Q8_0 activation (and fp32 copy) in shared memory ----
     if (IN == IN_QUANT) {
@@ -182,22 +237,14 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
     } else {
         for (int i = tid; i < cols; i += GEMV_THREADS) xf_s[i] = a.x[i];
         if (IN == IN_NORM) {
-            // RMSNorm (ref src/model.c:50-55): products in parallel, then the sum of
-            // squares as ONE sequential chain in index order, as the reference adds.
-            float *sq = P;
+            // RMSNorm (ref src/model.c:50-55): the sum of squares as ONE sequential
+            // chain in index order, as the reference adds
             __syncthreads();
-            for (int i = tid; i < cols; i += GEMV_THREADS) sq[i] = fmul(xf_s[i], xf_s[i]);
-            __syncthreads();
-            if (tid == 0) {
-                float ss = 0.0f;
-#pragma unroll 16
-                for (int i = 0; i < cols; i++) ss = fadd(ss, sq[i]);
-                s_scale = rms_scale(ss, cols, a.eps);
-            }
+            if (tid == 0) s_scale = rms_scale(chain_sumsq(xf_s, cols), cols, a.eps);
             __syncthreads();
             const float sc = s_scale;
             for (int i = tid; i < cols; i += GEMV_THREADS)
-                xf_s[i] = fmul(fmul(xf_s[i], sc), a.norm_w[i]);   // (x*scale)*w
+                xf_s[i] = fmul(fmul(xf_s[i], sc), nw_s[i]);   // (x*scale)*w
         }
         __syncthreads();
         // quantize the activation, one warp per 32-block (ref src/kernels.c:211)
@@ -216,76 +263,78 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
     __syncthreads();
 
     // ---- tiles ----
-    int k = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        int nsub, row0;
-        GemvSeg g0, g1;
-        if (EPI == EPI_SWIGLU) {
-            g0 = a.seg[0];
-            g1 = a.seg[1];
-            row0 = t * GEMV_ROWS;
-            nsub = 2;
-        } else {
-            while (k + 1 < a.nseg && t >= a.tiles[k + 1]) k++;
-            g0 = pick_seg(a, k);
-            g1 = g0;
-            row0 = (t - a.tiles[k]) * GEMV_ROWS;
-            nsub = 1;
-        }
-        (void)ntiles_seg;
-        const int nrows = min(GEMV_ROWS, g0.rows - row0);
-        const int rows_total = nsub * GEMV_ROWS;
+    for (int k = 0; k < my_tiles; k++) {
+        const int t = blockIdx.x + k * gridDim.x;
+        TileRef tr[nsub];
+#pragma unroll
+        for (int sub = 0; sub < nsub; sub++) tr[sub] = tile_ref<EPI>(a, t, sub);
+        const int nrows = tr[0].nrows;
 
-        // phase 1: per (row, block) products ((float)acc * d_w) * d_x into P
-        for (int sub = 0; sub < nsub; sub++) {
-            const GemvSeg &g = sub == 0 ? g0 : g1;
-            if (g.dtype == EMBER_DT_F32) {
-                // fp32 weights: the reference's scalar dot, one chain per row over
-                // all inputs in order (ref src/kernels.c:143-146)
-                if (tid < nrows) {
-                    const float *w = reinterpret_cast<const float *>(g.q) + (size_t)(row0 + tid) * cols;
+        if (S > 0) {
+            const int st = k % S;
+            const unsigned char *stage = stage0 + (size_t)st * a.stage_bytes;
+            mbar_wait_cta(&bars[st], (uint32_t)((k / S) & 1), a.err, ERR_GEMV_WAIT);
+            // phase 1: per (row, block) terms ((float)acc * d_w) * d_x into P
+            size_t soff = 0;
+#pragma unroll
+            for (int sub = 0; sub < nsub; sub++) {
+                const GemvSeg &g = tr[sub].g;
+                const size_t rb = qrow_bytes(g.dtype, cols);
+                const uint8_t *tq = stage + soff;
+                const __half *ts = reinterpret_cast<const __half *>(stage + soff + pad16((size_t)R * rb));
+                const int items = tr[sub].nrows * nb;
+                float *Ps = P + (size_t)sub * GEMV_MAX_ROWS * pstride;
+                if (g.dtype == EMBER_DT_Q8_0) {
+                    for (int j = tid; j < items; j += GEMV_THREADS) {
+                        const int r = j / nb, b = j - r * nb;
+                        int acc = dot_q8_block(tq + (size_t)r * rb + (size_t)b * 32, xq_s + b * 32);
+                        Ps[r * pstride + b] = fmul(fmul(__int2float_rn(acc), __half2float(ts[j])), xd_s[b]);
+                    }
+                } else {
+                    for (int j = tid; j < items; j += GEMV_THREADS) {
+                        const int r = j / nb, b = j - r * nb;
+                        int acc = dot_q4_block(tq + (size_t)r * rb + (size_t)b * 16, xq_s + b * 32);
+                        Ps[r * pstride + b] = fmul(fmul(__int2float_rn(acc), __half2float(ts[j])), xd_s[b]);
+                    }
+                }
+                soff += gemv_sub_bytes(g.dtype, R, cols);
+            }
+            __syncthreads();
+            // the stage is free: refill it with this CTA's tile k + S
+            if (tid == 0 && k + S < my_tiles) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue_tile<EPI>(a, blockIdx.x + (k + S) * gridDim.x, stage0 + (size_t)st * a.stage_bytes, &bars[st]);
+            }
+            // phase 2: each row's block terms summed in block order (ref src/kernels.c:152-164)
+            if (tid < nsub * R) {
+                const int sub = tid / R, r = tid - sub * R;
+                if (r < tr[sub].nrows) {
+                    const float *pr = P + ((size_t)sub * GEMV_MAX_ROWS + r) * pstride;
+                    rowsum[sub * GEMV_MAX_ROWS + r] = chain_sum(0.0f, pr, nb);
+                }
+            }
+        } else {
+            // fp32 weights: the reference's scalar dot, one chain per row over
+            // all inputs in order (ref src/kernels.c:143-146)
+            if (tid < nsub * R) {
+                const int sub = tid / R, r = tid - sub * R;
+                if (r < tr[sub].nrows) {
+                    const float *w = reinterpret_cast<const float *>(tr[sub].g.q) + (size_t)(tr[sub].row0 + r) * cols;
                     float s = 0.0f;
                     for (int i = 0; i < cols; i++) s = fadd(s, fmul(__ldg(w + i), xf_s[i]));
-                    rowsum[sub * GEMV_ROWS + tid] = s;
+                    rowsum[sub * GEMV_MAX_ROWS + r] = s;
                 }
-                continue;
-            }
-            const size_t rb = qrow_bytes(g.dtype, cols);
-            const uint8_t *tq = g.q + rb * (size_t)row0;
-            const __half *ts = g.s + (size_t)row0 * nb;
-            const int items = nrows * nb;
-            const int bbytes = g.dtype == EMBER_DT_Q8_0 ? 32 : 16;
-            float *Ps = P + (size_t)sub * GEMV_ROWS * pstride;
-            for (int j = tid; j < items; j += GEMV_THREADS) {
-                const int r = j / nb, b = j - r * nb;
-                const uint8_t *wb = tq + (size_t)r * rb + (size_t)b * bbytes;
-                int acc = g.dtype == EMBER_DT_Q8_0 ? dot_q8_block(wb, xq_s + b * 32)
-                                                   : dot_q4_block(wb, xq_s + b * 32);
-                float dw = __half2float(ts[j]);
-                Ps[r * pstride + b] = fmul(fmul(__int2float_rn(acc), dw), xd_s[b]);
-            }
-        }
-        __syncthreads();
-        // phase 2: each row's block terms summed in block order (ref src/kernels.c:152-164)
-        if (tid < rows_total) {
-            const int sub = tid / GEMV_ROWS, r = tid - sub * GEMV_ROWS;
-            const GemvSeg &g = sub == 0 ? g0 : g1;
-            if (r < nrows && g.dtype != EMBER_DT_F32) {
-                const float *pr = P + ((size_t)sub * GEMV_ROWS + r) * pstride;
-                float s = 0.0f;
-#pragma unroll 8
-                for (int b = 0; b < nb; b++) s = fadd(s, pr[b]);
-                rowsum[tid] = s;
             }
         }
         __syncthreads();
         // epilogue
+        const int row0 = tr[0].row0;
         if (EPI == EPI_SWIGLU) {
             if (tid < 32) {
                 // h = SiLU(g) * u = g / (1 + expf(-g)) * u (ref src/model.c:403-406)
                 float h = 0.0f;
                 if (tid < nrows) {
-                    float gv = rowsum[tid], uv = rowsum[GEMV_ROWS + tid];
+                    float gv = rowsum[tid], uv = rowsum[GEMV_MAX_ROWS + tid];
                     float e = expf_exact(a.ex, -gv);
                     h = fmul(fdiv(gv, fadd(1.0f, e)), uv);
                     if (a.hf) a.hf[row0 + tid] = h;
@@ -298,11 +347,12 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
             }
         } else if (tid < nrows) {
             float s = rowsum[tid];
+            const GemvSeg &g = tr[0].g;
             if (EPI == EPI_RESID) {
-                g0.out[row0 + tid] = fadd(g0.out[row0 + tid], s);    // x += y (ref :398, :408)
+                g.out[row0 + tid] = fadd(g.out[row0 + tid], s);    // x += y (ref :398, :408)
             } else {
-                if (g0.bias) s = fadd(s, g0.bias[row0 + tid]);
-                g0.out[row0 + tid] = s;
+                if (g.bias) s = fadd(s, g.bias[row0 + tid]);
+                g.out[row0 + tid] = s;
             }
         }
         __syncthreads();
@@ -313,54 +363,113 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
 
 struct AttnArgs {
     const float *q, *k, *v;        // this position's projections (bias already added)
-    void *kc, *vc;                 // this layer's cache: [n_kv][ctx][hd], fp32 or fp16
+    void *kc;                      // this layer's keys, transposed: [n_kv][hd][kstride]
+    void *vc;                      // this layer's values: [n_kv][ctx][hd]
     const float *q_norm, *k_norm;  // QK-norm weights [hd] or NULL
     const float2 *rope;            // [ctx][hd/2] (cos, sin)
-    const int *ctl;
-    float *att;                    // scratch [n_heads][ctx]
+    int *ctl;
+    float *att;                    // global scores [n_heads][ctx] when they do not fit smem
     int8_t *oq;                    // outputs: Q8 of the head outputs [n_heads*hd] ...
     float *od;                     //   ... their scales [n_heads*hd/32]
-    float *of;                     //   ... and the fp32 values
-    int nh, nkv, hd, ctx, neox;
+    float *of;                     //   ... and the fp32 values (may be NULL)
+    int nh, nkv, hd, ctx, kstride, neox, att_in_smem;
+    int chunk;                     // cached positions per staged chunk
     float eps;
     ExpfDev ex;
 };
 
-EMB_DEV float kv_load(const float *p) { return *p; }
-EMB_DEV float kv_load(const __half *p) { return __half2float(*p); }
-
-EMB_DEV void kv_load4(const float *p, float *o) {
-    float4 v = *reinterpret_cast<const float4 *>(p);
-    o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
-}
-EMB_DEV void kv_load4(const __half *p, float *o) {
-    uint2 u = *reinterpret_cast<const uint2 *>(p);
-    __half2 a = *reinterpret_cast<__half2 *>(&u.x), b = *reinterpret_cast<__half2 *>(&u.y);
-    float2 fa = __half22float2(a), fb = __half22float2(b);
-    o[0] = fa.x; o[1] = fa.y; o[2] = fb.x; o[3] = fb.y;
-}
-
+EMB_DEV float widen(float v) { return v; }
+EMB_DEV float widen(__half v) { return __half2float(v); }
 // the value stored in the cache: fp32 as is, or fp16 rounded to nearest even
 // (ref src/model.c:43, ember_f16c)
 EMB_DEV void kv_round(float v, float *out) { *out = v; }
 EMB_DEV void kv_round(float v, __half *out) { *out = __float2half_rn(v); }
-EMB_DEV float kv_widen(float v) { return v; }
-EMB_DEV float kv_widen(__half v) { return __half2float(v); }
+
+// Copy keys of positions [c0, c0+n) (all hd rows of the transposed layout) into
+// kbuf[hd][CH] with 16-byte loads by all threads, eight in flight per thread.
+// Rows are padded to kstride, so rounding n up to a vector stays in bounds.
+template <typename T>
+EMB_DEV void load_k_chunk(T *kbuf, const T *kt, int kstride, int c0, int n, int hd, int CH) {
+    constexpr int E = 16 / (int)sizeof(T);
+    const int nv = (n + E - 1) / E;
+    const int total = hd * nv;
+    for (int base = threadIdx.x; base < total; base += ATTN_THREADS * 8) {
+        int4 r[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int idx = base + u * ATTN_THREADS;
+            if (idx < total) {
+                const int i = idx / nv, vv = idx - i * nv;
+                r[u] = *reinterpret_cast<const int4 *>(kt + (size_t)i * kstride + c0 + vv * E);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int idx = base + u * ATTN_THREADS;
+            if (idx < total) {
+                const int i = idx / nv, vv = idx - i * nv;
+                *reinterpret_cast<int4 *>(kbuf + (size_t)i * CH + vv * E) = r[u];
+            }
+        }
+    }
+}
 
 // One query position over the cache for one head (ref src/model.c:221-259).
+//
+// Pre-wait (data of earlier launches only): the position word, the QK-norm
+// weights, this position's cos/sin, the first chunk of cached keys (thread
+// loads into a transposed [hd][chunk] buffer) and values (one bulk copy into a
+// [chunk][hd] buffer). Post-wait: this position's q/k/v from the projection,
+// QK-norm and RoPE, the KV store, then
+//   scores  one thread per cached position: sum_i q_i*k_i in index order;
+//   softmax max (order-free), expf, the sequential sum, the reciprocal;
+//   output  one thread per dimension: sum_t w_t*v_t in position order,
+// each chain reading shared memory with its loads batched ahead of the adds.
+// Further value chunks ping-pong between the two buffers by bulk copies.
 template <typename T>
 __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArgs a) {
-    __shared__ float qs[256], ks[256], vs[256];
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ float qs[256], ks[256], vs[256], qn_s[256], kn_s[256];
+    __shared__ float2 cs_s[128];
     __shared__ float red[ATTN_THREADS / 32];
     __shared__ float s_q, s_k, s_max, s_inv;
-    const int h = blockIdx.x, tid = threadIdx.x, hd = a.hd;
-    const int kvh = h / (a.nh / a.nkv);
-    pdl_launch_dependents();
-    pdl_wait();
-    const int pos = a.ctl[CTL_POS];
-    T *kc = reinterpret_cast<T *>(a.kc) + (size_t)kvh * a.ctx * hd;
-    T *vc = reinterpret_cast<T *>(a.vc) + (size_t)kvh * a.ctx * hd;
+    const int h = blockIdx.x, tid = threadIdx.x, hd = a.hd, CH = a.chunk;
+    const int kv_mul = a.nh / a.nkv, kvh = h / kv_mul;
+    const int warp = tid >> 5, lane = tid & 31;
+    const size_t buf_elems = (size_t)CH * hd;
+    T *buf0 = reinterpret_cast<T *>(smem);
+    T *buf1 = buf0 + buf_elems;
+    float *att = a.att_in_smem ? reinterpret_cast<float *>(smem + 2 * buf_elems * sizeof(T))
+                               : a.att + (size_t)h * a.ctx;
+    int *err = a.ctl + CTL_ERR;
+    uint32_t ph0 = 0, ph1 = 0;
 
+    // ---- pre-wait ----
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+    }
+    const int pos = a.ctl[CTL_POS];   // written by the host or the previous step's tail
+    T *kt = reinterpret_cast<T *>(a.kc) + (size_t)kvh * hd * a.kstride;
+    T *vt = reinterpret_cast<T *>(a.vc) + (size_t)kvh * a.ctx * hd;
+    if (tid < hd) {
+        qn_s[tid] = a.q_norm ? a.q_norm[tid] : 0.0f;
+        kn_s[tid] = a.k_norm ? a.k_norm[tid] : 0.0f;
+    }
+    if (tid < hd / 2) cs_s[tid] = a.rope[(size_t)pos * (hd / 2) + tid];
+    __syncthreads();
+    const int nchunks = (pos + CH - 1) / CH;
+    const int n0 = min(CH, pos);
+    if (tid == 0 && n0 > 0) {         // values of chunk 0 -> buf1
+        mbar_expect_tx(&bars[1], (uint32_t)(n0 * hd * (int)sizeof(T)));
+        bulk_g2s(buf1, vt, (uint32_t)(n0 * hd * sizeof(T)), &bars[1]);
+    }
+    if (n0 > 0) load_k_chunk(buf0, kt, a.kstride, 0, n0, hd, CH);   // keys of chunk 0 -> buf0
+    pdl_wait_then_release();
+
+    // ---- this position: q, k, v; QK-norm; RoPE; KV store ----
     if (tid < hd) {
         qs[tid] = a.q[h * hd + tid];
         ks[tid] = a.k[kvh * hd + tid];
@@ -370,26 +479,19 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
     if (a.q_norm) {
         // per-head RMSNorm of q and k, in place (ref src/model.c:386-389); the two
         // sequential sums run on different warps
-        if (tid == 0) {
-            float ss = 0.0f;
-            for (int i = 0; i < hd; i++) ss = fadd(ss, fmul(qs[i], qs[i]));
-            s_q = rms_scale(ss, hd, a.eps);
-        } else if (tid == 32) {
-            float ss = 0.0f;
-            for (int i = 0; i < hd; i++) ss = fadd(ss, fmul(ks[i], ks[i]));
-            s_k = rms_scale(ss, hd, a.eps);
-        }
+        if (tid == 0) s_q = rms_scale(chain_sumsq(qs, hd), hd, a.eps);
+        else if (tid == 32) s_k = rms_scale(chain_sumsq(ks, hd), hd, a.eps);
         __syncthreads();
         if (tid < hd) {
-            qs[tid] = fmul(fmul(qs[tid], s_q), a.q_norm[tid]);
-            ks[tid] = fmul(fmul(ks[tid], s_k), a.k_norm[tid]);
+            qs[tid] = fmul(fmul(qs[tid], s_q), qn_s[tid]);
+            ks[tid] = fmul(fmul(ks[tid], s_k), kn_s[tid]);
         }
         __syncthreads();
     }
     // RoPE (ref src/model.c:66-80) with the host-built cos/sin table
     if (tid < hd / 2) {
         const int ia = a.neox ? tid : 2 * tid, ib = a.neox ? tid + hd / 2 : 2 * tid + 1;
-        const float2 cs = a.rope[(size_t)pos * (hd / 2) + tid];
+        const float2 cs = cs_s[tid];
         float v0 = qs[ia], v1 = qs[ib];
         qs[ia] = fsub(fmul(v0, cs.x), fmul(v1, cs.y));
         qs[ib] = fadd(fmul(v0, cs.y), fmul(v1, cs.x));
@@ -398,47 +500,61 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
         ks[ib] = fadd(fmul(v0, cs.y), fmul(v1, cs.x));
     }
     __syncthreads();
-    // KV store (ref src/model.c:39-48): the cache holds fp32 or RNE fp16; attention
-    // reads the stored values, including at t == pos
+    // KV store (ref src/model.c:39-48): the cache holds fp32 or RNE fp16, and
+    // attention reads the stored values, including at t == pos
     if (tid < hd) {
-        T kt, vt;
-        kv_round(ks[tid], &kt);
-        kv_round(vs[tid], &vt);
-        ks[tid] = kv_widen(kt);
-        vs[tid] = kv_widen(vt);
-        if (h % (a.nh / a.nkv) == 0) {
-            kc[(size_t)pos * hd + tid] = kt;
-            vc[(size_t)pos * hd + tid] = vt;
+        T kq, vq;
+        kv_round(ks[tid], &kq);
+        kv_round(vs[tid], &vq);
+        ks[tid] = widen(kq);
+        vs[tid] = widen(vq);
+        if (h % kv_mul == 0) {
+            kt[(size_t)tid * a.kstride + pos] = kq;
+            vt[(size_t)pos * hd + tid] = vq;
         }
     }
     __syncthreads();
 
-    // scores: sc = sum_i q_i*k_i in index order, then * (1/sqrt(hd))
+    // ---- scores: sc = sum_i q_i*k_i in index order, then * (1/sqrt(hd)) ----
     const float inv_sqrt = fdiv(1.0f, fsqrt((float)hd));
-    float *att = a.att + (size_t)h * a.ctx;
-    float tmax = -INFINITY;
-    for (int t = tid; t <= pos; t += ATTN_THREADS) {
-        float sc = 0.0f;
-        if (t == pos) {
-            for (int i = 0; i < hd; i++) sc = fadd(sc, fmul(qs[i], ks[i]));
-        } else {
-            const T *kr = kc + (size_t)t * hd;
-            for (int i = 0; i < hd; i += 4) {
-                float kk[4];
-                kv_load4(kr + i, kk);
-                sc = fadd(sc, fmul(qs[i], kk[0]));
-                sc = fadd(sc, fmul(qs[i + 1], kk[1]));
-                sc = fadd(sc, fmul(qs[i + 2], kk[2]));
-                sc = fadd(sc, fmul(qs[i + 3], kk[3]));
-            }
+    for (int c = 0; c < nchunks; c++) {
+        const int c0 = c * CH, n = min(CH, pos - c0);
+        if (c > 0) {
+            __syncthreads();
+            load_k_chunk(buf0, kt, a.kstride, c0, n, hd, CH);
+            __syncthreads();
         }
-        sc = fmul(sc, inv_sqrt);
-        att[t] = sc;
-        tmax = fmaxf(tmax, sc);
+        for (int t = tid; t < n; t += ATTN_THREADS) {
+            float sc = 0.0f;
+            for (int i = 0; i < hd; i += 8) {
+                float kk[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) kk[j] = widen(buf0[(size_t)(i + j) * CH + t]);
+#pragma unroll
+                for (int j = 0; j < 8; j++) sc = fadd(sc, fmul(qs[i + j], kk[j]));
+            }
+            att[c0 + t] = fmul(sc, inv_sqrt);
+        }
     }
-    // softmax (ref src/model.c:57-64): max is order-free
+    if (tid == 0) {
+        float sc = 0.0f;
+        for (int i = 0; i < hd; i++) sc = fadd(sc, fmul(qs[i], ks[i]));
+        att[pos] = fmul(sc, inv_sqrt);
+    }
+    __syncthreads();
+    // the keys are done: value chunk 1 may stream into buf0 during the softmax
+    if (tid == 0 && nchunks > 1) {
+        const int n1 = min(CH, pos - CH);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(&bars[0], (uint32_t)(n1 * hd * (int)sizeof(T)));
+        bulk_g2s(buf0, vt + (size_t)CH * hd, (uint32_t)(n1 * hd * sizeof(T)), &bars[0]);
+    }
+
+    // ---- softmax (ref src/model.c:57-64): the max is order-free ----
+    float tmax = -INFINITY;
+    for (int t = tid; t <= pos; t += ATTN_THREADS) tmax = fmaxf(tmax, att[t]);
     tmax = warp_max(tmax);
-    if ((tid & 31) == 0) red[tid >> 5] = tmax;
+    if (lane == 0) red[warp] = tmax;
     __syncthreads();
     if (tid == 0) {
         float m = red[0];
@@ -449,30 +565,49 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
     const float mx = s_max;
     for (int t = tid; t <= pos; t += ATTN_THREADS) att[t] = expf_exact(a.ex, fsub(att[t], mx));
     __syncthreads();
-    if (tid == 0) {
-        float sum = 0.0f;                            // sequential, t = 0..pos
-#pragma unroll 8
-        for (int t = 0; t <= pos; t++) sum = fadd(sum, att[t]);
-        s_inv = fdiv(1.0f, sum);
-    }
+    if (tid == 0) s_inv = fdiv(1.0f, chain_sum(0.0f, att, pos + 1));   // sequential, t = 0..pos
     __syncthreads();
     const float inv = s_inv;
     for (int t = tid; t <= pos; t += ATTN_THREADS) att[t] = fmul(att[t], inv);
     __syncthreads();
 
-    // out_i = sum_t w_t * v_t,i, sequential over t (ref src/model.c:252-256)
+    // ---- out_i = sum_t w_t * v_t,i, sequential over t (ref src/model.c:252-256) ----
+    float o = 0.0f;
+    for (int c = 0; c < nchunks; c++) {
+        const int c0 = c * CH, n = min(CH, pos - c0);
+        const bool in1 = (c & 1) == 0;           // chunks 0,2,4.. in buf1; 1,3,.. in buf0
+        T *vb = in1 ? buf1 : buf0;
+        if (in1) { mbar_wait_cta(&bars[1], ph1, err, ERR_ATTN_WAIT); ph1 ^= 1; }
+        else     { mbar_wait_cta(&bars[0], ph0, err, ERR_ATTN_WAIT); ph0 ^= 1; }
+        if (tid < hd) {
+            const float *w = att + c0;
+            int t = 0;
+            for (; t + 8 <= n; t += 8) {
+                float ww[8], vv[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) { ww[j] = w[t + j]; vv[j] = widen(vb[(size_t)(t + j) * hd + tid]); }
+#pragma unroll
+                for (int j = 0; j < 8; j++) o = fadd(o, fmul(ww[j], vv[j]));
+            }
+            for (; t < n; t++) o = fadd(o, fmul(w[t], widen(vb[(size_t)t * hd + tid])));
+        }
+        __syncthreads();
+        if (tid == 0 && c + 2 < nchunks) {       // refill the freed buffer with chunk c+2
+            const int n2 = min(CH, pos - (c + 2) * CH);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            uint64_t *bb = in1 ? &bars[1] : &bars[0];
+            mbar_expect_tx(bb, (uint32_t)(n2 * hd * (int)sizeof(T)));
+            bulk_g2s(vb, vt + (size_t)(c + 2) * CH * hd, (uint32_t)(n2 * hd * sizeof(T)), bb);
+        }
+    }
     if (tid < hd) {
-        float o = 0.0f;
-        const T *vcol = vc + tid;
-#pragma unroll 8
-        for (int t = 0; t < pos; t++) o = fadd(o, fmul(att[t], kv_load(vcol + (size_t)t * hd)));
         o = fadd(o, fmul(att[pos], vs[tid]));
         const int gi = h * hd + tid;
         if (a.of) a.of[gi] = o;
         float dq;
         int8_t q = quant_lane(o, &dq);   // hd % 32 == 0: each warp owns one block
         a.oq[gi] = q;
-        if ((tid & 31) == 0) a.od[gi / 32] = dq;
+        if (lane == 0) a.od[gi / 32] = dq;
     }
 }
 
@@ -489,8 +624,7 @@ struct EmbedArgs {
 
 // x = the token's embedding row, dequantized as q*d (ref src/model.c:83-100)
 __global__ void __launch_bounds__(256) embed_kernel(const EmbedArgs a) {
-    pdl_launch_dependents();
-    pdl_wait();
+    pdl_wait_then_release();
     const int pos = a.ctl[CTL_POS];
     const int tok = a.ids ? a.ids[pos - a.ctl[CTL_BASE]] : a.ctl[CTL_TOK];
     for (int i = threadIdx.x; i < a.dim; i += blockDim.x) {
@@ -525,8 +659,7 @@ __global__ void __launch_bounds__(256) argmax_advance_kernel(const ArgmaxArgs a)
     __shared__ float sv[256];
     __shared__ int si[256];
     __shared__ bool last;
-    pdl_launch_dependents();
-    pdl_wait();
+    pdl_wait_then_release();
     float bv = -INFINITY;
     int bi = 0x7FFFFFFF;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += gridDim.x * blockDim.x)
@@ -574,8 +707,7 @@ __global__ void __launch_bounds__(256) argmax_advance_kernel(const ArgmaxArgs a)
 
 // prefill bookkeeping between steps: advance the position
 __global__ void advance_kernel(int *ctl) {
-    pdl_launch_dependents();
-    pdl_wait();
+    pdl_wait_then_release();
     if (threadIdx.x == 0) ctl[CTL_POS] += 1;
 }
 

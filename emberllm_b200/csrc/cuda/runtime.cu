@@ -4,18 +4,19 @@
 // Device layout. A .ember Q8_0 row is an array of 34-byte {fp16 d; int8 qs[32]}
 // blocks (18-byte for Q4_0), so rows are not 16-byte aligned and scales sit
 // between the quants. At upload every quantized matrix is split into a
-// row-major byte array (32 or 16 bytes per block, every row and block 16-byte
-// aligned, so a warp streams a tile of consecutive rows with 128-bit loads) and
-// a separate [rows][cols/32] fp16 scale array. The KV cache is laid out per
-// layer as [n_kv][ctx][head_dim] so one head's keys for consecutive positions
-// are contiguous.
+// row-major byte array (32 or 16 bytes per block, every row 16-byte aligned) and
+// a separate [rows][cols/32] fp16 scale array; a tile of R consecutive rows is
+// then two contiguous byte ranges, each moved by one bulk copy. The KV cache is
+// per layer and kv head: keys TRANSPOSED, [hd][kstride] (kstride = ctx rounded
+// up to 8), so one thread per position reads consecutive addresses per
+// dimension; values [ctx][hd].
 //
 // Execution. One token step is a fixed sequence of kernels (kernels.cuh) that
 // read the position and token from device memory, captured once per state into
 // CUDA graphs and replayed for every token. Kernels are launched with
 // programmatic stream serialization so each one starts while its predecessor
-// finishes and prefetches its own weights into L2 before waiting on the data it
-// needs.
+// finishes and pulls its own weights into shared memory before waiting on the
+// data it needs.
 #include <cuda_runtime.h>
 
 #include <stdarg.h>
@@ -75,6 +76,22 @@ extern "C" int ember_cuda_available(void) {
     return p.major >= 10;
 }
 
+// Raise the dynamic shared-memory limit of every kernel instantiation once per
+// device, outside any stream capture.
+static int init_kernel_attrs(int device) {
+    static unsigned done_mask = 0;
+    if (device < 32 && ((done_mask >> device) & 1u)) return 0;
+    const int lim = 220 * 1024;
+    CK(cudaFuncSetAttribute(gemv_kernel<IN_RAW, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+    CK(cudaFuncSetAttribute(gemv_kernel<IN_NORM, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+    CK(cudaFuncSetAttribute(gemv_kernel<IN_NORM, EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+    CK(cudaFuncSetAttribute(gemv_kernel<IN_QUANT, EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+    CK(cudaFuncSetAttribute(attn_decode_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+    CK(cudaFuncSetAttribute(attn_decode_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+    if (device < 32) done_mask |= 1u << device;
+    return 0;
+}
+
 // ------------------------------------------------------------------ model -----
 
 struct DevMat {
@@ -91,8 +108,9 @@ struct DevLayer {
 
 struct EmberCudaModel {
     int device = 0, n_sm = 148;
-    int dim, hidden, n_layers, n_heads, n_kv, head_dim, vocab, qk_norm, rope_neox;
-    float eps;
+    int dim = 0, hidden = 0, n_layers = 0, n_heads = 0, n_kv = 0, head_dim = 0, vocab = 0;
+    int qk_norm = 0, rope_neox = 0;
+    float eps = 0;
     DevMat tok_emb, lm_head;
     float *final_norm = nullptr;
     std::vector<DevLayer> layers;
@@ -115,7 +133,8 @@ static int upload_vec(EmberCudaModel *m, float **dst, const float *src, int n) {
     return 0;
 }
 
-// Split AoS blocks into quant rows + scale rows and upload.
+// Split AoS blocks into quant rows + scale rows and upload. The scale array is
+// padded by 256 bytes: tile copies round their size up to 16 bytes.
 static int upload_mat(EmberCudaModel *m, DevMat *d, const EmberCudaMat &h) {
     d->dtype = h.dtype;
     d->rows = h.rows;
@@ -130,8 +149,8 @@ static int upload_mat(EmberCudaModel *m, DevMat *d, const EmberCudaMat &h) {
     const int nb = h.cols / 32;
     const size_t blk_in = h.dtype == EMBER_DT_Q8_0 ? 34 : 18, blk_q = blk_in - 2;
     const size_t qn = rows * nb * blk_q, sn = rows * nb * 2;
-    if (dalloc(m, (void **)&d->q, qn) || dalloc(m, (void **)&d->s, sn)) return 1;
-    // repack in row chunks to bound the host staging buffer
+    if (dalloc(m, (void **)&d->q, qn) || dalloc(m, (void **)&d->s, sn + 256)) return 1;
+    CK(cudaMemset(d->s, 0, sn + 256));
     const size_t chunk_rows = 4096;
     std::vector<uint8_t> qb(chunk_rows * nb * blk_q);
     std::vector<uint16_t> sb(chunk_rows * nb);
@@ -214,19 +233,23 @@ extern "C" uint64_t ember_cuda_model_bytes(const EmberCudaModel *m) { return m ?
 
 struct EmberCudaState {
     EmberCudaModel *m = nullptr;
-    int ctx = 0, kv_fp16 = 0;
+    int ctx = 0, kv_fp16 = 0, kstride = 0;
     cudaStream_t stream = nullptr;
     std::vector<void *> allocs;
     // device buffers
-    float *x, *q, *k, *v, *att, *od, *of, *hd, *hf, *logits;
-    int8_t *oq, *hq;
-    void *kc, *vc;
-    float2 *rope;
-    int *ctl, *ids, *out_tokens;
-    float *am_v;
-    int *am_i;
-    unsigned *am_ticket;
-    int am_blocks;
+    float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr;
+    float *od = nullptr, *of = nullptr, *hd = nullptr, *hf = nullptr, *logits = nullptr;
+    int8_t *oq = nullptr, *hq = nullptr;
+    void *kc = nullptr, *vc = nullptr;
+    size_t k_layer_elems = 0, v_layer_elems = 0;
+    float2 *rope = nullptr;
+    int *ctl = nullptr, *ids = nullptr, *out_tokens = nullptr;
+    float *am_v = nullptr;
+    int *am_i = nullptr;
+    unsigned *am_ticket = nullptr;
+    int am_blocks = 0;
+    int att_in_smem = 0, attn_chunk = 0;
+    size_t attn_smem = 0;
     // pinned host
     float *h_logits = nullptr;
     int *h_ctl = nullptr;
@@ -234,8 +257,6 @@ struct EmberCudaState {
     cudaGraphExec_t g_fwd = nullptr, g_greedy = nullptr, g_prefill = nullptr, g_head = nullptr;
     int launches_per_step = 0;
 };
-
-static int init_kernel_attrs(int device);
 
 static int salloc(EmberCudaState *s, void **p, size_t n) {
     CK(cudaMalloc(p, n ? n : 16));
@@ -264,25 +285,41 @@ extern "C" int ember_cuda_state_new(EmberCudaModel *m, int ctx, int kv_fp16, con
     s->m = m;
     s->ctx = ctx;
     s->kv_fp16 = kv_fp16;
+    s->kstride = (ctx + 7) / 8 * 8;
     const int hd = m->head_dim, qd = m->n_heads * hd, kvd = m->n_kv * hd;
     const size_t es = kv_fp16 ? 2 : 4;
-    const size_t kv_bytes = (size_t)m->n_layers * ctx * kvd * es;
+    s->k_layer_elems = (size_t)m->n_kv * hd * s->kstride;
+    s->v_layer_elems = (size_t)m->n_kv * ctx * hd;
+    const size_t k_bytes = (size_t)m->n_layers * s->k_layer_elems * es + 256;
+    const size_t v_bytes = (size_t)m->n_layers * s->v_layer_elems * es + 256;
     s->am_blocks = m->n_sm;
+    // attention shared memory: two chunk buffers (keys/values of `attn_chunk`
+    // cached positions each) and, when they fit, the scores of all positions
+    {
+        const size_t budget = 200 * 1024, att_bytes = pad16((size_t)ctx * 4);
+        s->att_in_smem = att_bytes <= 48 * 1024;
+        const size_t for_bufs = budget - (s->att_in_smem ? att_bytes : 0);
+        int chunk = (int)(for_bufs / (2 * (size_t)hd * es)) / 8 * 8;
+        if (chunk > 1024) chunk = 1024;
+        if (chunk < 8) chunk = 8;
+        s->attn_chunk = chunk;
+        s->attn_smem = 2 * (size_t)chunk * hd * es + (s->att_in_smem ? att_bytes : 0);
+    }
     int rc = 0;
     rc |= salloc(s, (void **)&s->x, (size_t)m->dim * 4);
     rc |= salloc(s, (void **)&s->q, (size_t)qd * 4);
     rc |= salloc(s, (void **)&s->k, (size_t)kvd * 4);
     rc |= salloc(s, (void **)&s->v, (size_t)kvd * 4);
-    rc |= salloc(s, (void **)&s->att, (size_t)m->n_heads * ctx * 4);
-    rc |= salloc(s, (void **)&s->oq, (size_t)qd);
-    rc |= salloc(s, (void **)&s->od, (size_t)qd / 32 * 4 + 4);
+    rc |= salloc(s, (void **)&s->att, s->att_in_smem ? 16 : (size_t)m->n_heads * ctx * 4);
+    rc |= salloc(s, (void **)&s->oq, (size_t)qd + 16);
+    rc |= salloc(s, (void **)&s->od, (size_t)qd / 32 * 4 + 16);
     rc |= salloc(s, (void **)&s->of, (size_t)qd * 4);
     rc |= salloc(s, (void **)&s->hq, (size_t)m->hidden + 16);
-    rc |= salloc(s, (void **)&s->hd, (size_t)m->hidden / 32 * 4 + 4);
+    rc |= salloc(s, (void **)&s->hd, (size_t)m->hidden / 32 * 4 + 16);
     rc |= salloc(s, (void **)&s->hf, (size_t)m->hidden * 4);
     rc |= salloc(s, (void **)&s->logits, (size_t)m->vocab * 4);
-    rc |= salloc(s, &s->kc, kv_bytes);
-    rc |= salloc(s, &s->vc, kv_bytes);
+    rc |= salloc(s, &s->kc, k_bytes);
+    rc |= salloc(s, &s->vc, v_bytes);
     rc |= salloc(s, (void **)&s->rope, (size_t)ctx * (hd / 2) * sizeof(float2));
     rc |= salloc(s, (void **)&s->ctl, CTL_WORDS * 4);
     rc |= salloc(s, (void **)&s->ids, (size_t)ctx * 4);
@@ -301,7 +338,7 @@ extern "C" int ember_cuda_state_new(EmberCudaModel *m, int ctx, int kv_fp16, con
     }
     memset(s->h_ctl, 0, CTL_WORDS * 4);
     if (cudaMemcpy(s->rope, rope_cs, (size_t)ctx * (hd / 2) * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemset(s->kc, 0, kv_bytes) != cudaSuccess || cudaMemset(s->vc, 0, kv_bytes) != cudaSuccess ||
+        cudaMemset(s->kc, 0, k_bytes) != cudaSuccess || cudaMemset(s->vc, 0, v_bytes) != cudaSuccess ||
         cudaMemset(s->ctl, 0, CTL_WORDS * 4) != cudaSuccess || cudaMemset(s->am_ticket, 0, 4) != cudaSuccess ||
         cudaMemset(s->logits, 0, (size_t)m->vocab * 4) != cudaSuccess) {
         set_err("state initialisation failed: %s", cudaGetErrorString(cudaGetLastError()));
@@ -329,9 +366,28 @@ extern "C" int ember_cuda_state_launches_per_step(const EmberCudaState *s) { ret
 
 // ------------------------------------------------------------------ launches --
 
+// Profiling hook: when set, every launch of a step records an event first, so
+// ember_cuda_profile_step can report per-launch device times (no PDL overlap).
+static cudaEvent_t *g_prof_events = nullptr;
+static int g_prof_n = 0, g_prof_cap = 0;
+
+// EMBER_PDL=0 launches without programmatic dependent launch (for comparisons)
+static bool pdl_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("EMBER_PDL");
+        v = (e && *e == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
+
 template <typename... KArgs, typename... Args>
 static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_t smem, cudaStream_t st,
                               Args... args) {
+    if (g_prof_events && g_prof_n < g_prof_cap) {
+        cudaError_t e = cudaEventRecord(g_prof_events[g_prof_n++], st);
+        if (e != cudaSuccess) return e;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3((unsigned)block);
@@ -341,22 +397,8 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = (pdl_enabled() && !g_prof_events) ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kern, args...);
-}
-
-// Raise the dynamic shared-memory limit of every gemv instantiation once per
-// device, outside any stream capture.
-static int init_kernel_attrs(int device) {
-    static int done_mask = 0;
-    if (device < 31 && (done_mask >> device) & 1) return 0;
-    const int lim = 200 * 1024;
-    CK(cudaFuncSetAttribute(gemv_kernel<IN_RAW, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
-    CK(cudaFuncSetAttribute(gemv_kernel<IN_NORM, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
-    CK(cudaFuncSetAttribute(gemv_kernel<IN_NORM, EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
-    CK(cudaFuncSetAttribute(gemv_kernel<IN_QUANT, EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
-    if (device < 31) done_mask |= 1 << device;
-    return 0;
 }
 
 static GemvSeg seg_of(const DevMat &d, float *out, const float *bias) {
@@ -370,120 +412,202 @@ static GemvSeg seg_of(const DevMat &d, float *out, const float *bias) {
     return g;
 }
 
-static void gemv_tiles(GemvArgs &a) {
-    a.tiles[0] = 0;
-    for (int k = 0; k < a.nseg; k++) a.tiles[k + 1] = a.tiles[k] + (a.seg[k].rows + GEMV_ROWS - 1) / GEMV_ROWS;
-    for (int k = a.nseg + 1; k < 4; k++) a.tiles[k] = a.tiles[a.nseg];
-}
-
+// Choose the tile height, ring depth and grid of one gemv launch and launch it.
+// Segments must agree on being quantized (callers split otherwise).
 template <int IN, int EPI>
-static cudaError_t run_gemv(GemvArgs a, int n_sm, cudaStream_t st, int *count) {
+static int run_gemv(GemvArgs a, int n_sm, cudaStream_t st, int *count) {
+    const int nsub = EPI == EPI_SWIGLU ? 2 : 1;
+    a.quantized = a.seg[0].dtype != EMBER_DT_F32;
+    int rows_total = 0;
+    for (int k = 0; k < a.nseg; k++) rows_total += a.seg[k].rows;
+    // SwiGLU tiles are one quant block of h (32 rows); others shrink to spread
+    // small matrices over more SMs (R >= 8 keeps scale copies 16-byte aligned)
+    int R = GEMV_MAX_ROWS;
+    if (EPI != EPI_SWIGLU)
+        while (R > 8 && (rows_total + R - 1) / R < n_sm) R /= 2;
+    a.rows = R;
     if (EPI == EPI_SWIGLU) {
         a.tiles[0] = 0;
-        a.tiles[1] = a.tiles[2] = a.tiles[3] = (a.seg[0].rows + GEMV_ROWS - 1) / GEMV_ROWS;
-        a.nseg = 1;   // tiles[nseg] is the pair count; both segments are read per tile
+        a.tiles[1] = a.tiles[2] = a.tiles[3] = (a.seg[0].rows + R - 1) / R;
+        a.nseg = 1;   // tiles[nseg] counts pairs; both matrices are read per tile
     } else {
-        gemv_tiles(a);
+        a.tiles[0] = 0;
+        for (int k = 0; k < a.nseg; k++) a.tiles[k + 1] = a.tiles[k] + (a.seg[k].rows + R - 1) / R;
+        for (int k = a.nseg + 1; k < 4; k++) a.tiles[k] = a.tiles[a.nseg];
     }
     const int total = a.tiles[a.nseg];
-    int grid = total < 2 * n_sm ? total : 2 * n_sm;
+    size_t sb = 0;
+    for (int sub = 0; sub < nsub; sub++) sb += gemv_sub_bytes(a.seg[sub].dtype, R, a.cols);
+    a.stage_bytes = (int)((sb + 127) / 128 * 128);
+    // one CTA per tile for layer-sized matrices; a persistent ring for lm_head
+    int grid = total;
+    if (grid > 2 * n_sm) grid = 2 * n_sm;
     if (grid < 1) grid = 1;
     const int per_cta = (total + grid - 1) / grid;
-    a.prefetch_tiles = per_cta < 4 ? per_cta : 4;
-    bool f32 = false;
-    for (int k = 0; k < (EPI == EPI_SWIGLU ? 2 : a.nseg); k++) f32 |= a.seg[k].dtype == EMBER_DT_F32;
-    const size_t smem = gemv_smem_bytes(a.cols, IN != IN_QUANT || f32);
+    a.stages = a.quantized ? (per_cta < 3 ? per_cta : 3) : 0;
+    if (a.quantized && a.stages < 1) a.stages = 1;
+    const bool need_xf = IN != IN_QUANT || !a.quantized;
+    size_t smem = gemv_smem_bytes(a, need_xf);
+    while (a.quantized && smem > 200 * 1024 && a.stages > 1) {
+        a.stages--;
+        smem = gemv_smem_bytes(a, need_xf);
+    }
+    if (smem > 220 * 1024) return set_err("gemv tile of %d x %d does not fit shared memory", R, a.cols);
     if (count) (*count)++;
-    return launch_pdl(gemv_kernel<IN, EPI>, grid, GEMV_THREADS, smem, st, a);
+    CK(launch_pdl(gemv_kernel<IN, EPI>, grid, GEMV_THREADS, smem, st, a));
+    return 0;
+}
+
+static bool is_q(const DevMat &d) { return d.dtype != EMBER_DT_F32; }
+
+// ---- the launches of a token step, one helper per kernel kind ----
+
+enum { K_QKV = 0, K_ATTN = 1, K_WO = 2, K_W13 = 3, K_W2 = 4, K_HEAD = 5 };
+
+static int launch_embed(EmberCudaState *s, const int *ids, int *count) {
+    EmberCudaModel *m = s->m;
+    EmbedArgs ea;
+    ea.q = m->tok_emb.q; ea.s = m->tok_emb.s; ea.dtype = m->tok_emb.dtype; ea.dim = m->dim;
+    ea.ctl = s->ctl; ea.ids = ids; ea.x = s->x;
+    CK(launch_pdl(embed_kernel, 1, 256, 0, s->stream, ea));
+    (*count)++;
+    return 0;
+}
+
+static GemvArgs gemv_base(EmberCudaState *s) {
+    GemvArgs a;
+    memset(&a, 0, sizeof(a));
+    a.ex = s->m->ex;
+    a.err = s->ctl + CTL_ERR;
+    return a;
+}
+
+static int launch_layer(EmberCudaState *s, int kind, int l, int *count) {
+    EmberCudaModel *m = s->m;
+    cudaStream_t st = s->stream;
+    const DevLayer &L = m->layers[l];
+    const int hd = m->head_dim;
+    const size_t es = s->kv_fp16 ? 2 : 4;
+    GemvArgs a = gemv_base(s);
+    switch (kind) {
+    case K_QKV:
+        a.cols = m->dim;
+        a.x = s->x; a.norm_w = L.attn_norm; a.eps = m->eps;
+        if (is_q(L.wq) == is_q(L.wk) && is_q(L.wq) == is_q(L.wv)) {
+            a.seg[0] = seg_of(L.wq, s->q, L.bq);
+            a.seg[1] = seg_of(L.wk, s->k, L.bk);
+            a.seg[2] = seg_of(L.wv, s->v, L.bv);
+            a.nseg = 3;
+            return run_gemv<IN_NORM, EPI_STORE>(a, m->n_sm, st, count);
+        } else {
+            const DevMat *mats[3] = { &L.wq, &L.wk, &L.wv };
+            float *outs[3] = { s->q, s->k, s->v };
+            const float *bias[3] = { L.bq, L.bk, L.bv };
+            for (int j = 0; j < 3; j++) {
+                a.seg[0] = seg_of(*mats[j], outs[j], bias[j]);
+                a.nseg = 1;
+                if (run_gemv<IN_NORM, EPI_STORE>(a, m->n_sm, st, count)) return 1;
+            }
+            return 0;
+        }
+    case K_ATTN: {
+        AttnArgs at;
+        memset(&at, 0, sizeof(at));
+        at.q = s->q; at.k = s->k; at.v = s->v;
+        at.kc = (char *)s->kc + (size_t)l * s->k_layer_elems * es;
+        at.vc = (char *)s->vc + (size_t)l * s->v_layer_elems * es;
+        at.q_norm = L.q_norm; at.k_norm = L.k_norm;
+        at.rope = s->rope; at.ctl = s->ctl; at.att = s->att;
+        at.oq = s->oq; at.od = s->od; at.of = is_q(L.wo) ? nullptr : s->of;
+        at.nh = m->n_heads; at.nkv = m->n_kv; at.hd = hd; at.ctx = s->ctx; at.kstride = s->kstride;
+        at.neox = m->rope_neox; at.att_in_smem = s->att_in_smem; at.eps = m->eps; at.ex = m->ex;
+        at.chunk = s->attn_chunk;
+        if (s->kv_fp16) CK(launch_pdl(attn_decode_kernel<__half>, m->n_heads, ATTN_THREADS, s->attn_smem, st, at));
+        else CK(launch_pdl(attn_decode_kernel<float>, m->n_heads, ATTN_THREADS, s->attn_smem, st, at));
+        (*count)++;
+        return 0;
+    }
+    case K_WO:
+        a.cols = m->n_heads * hd;
+        a.xq = s->oq; a.xd = s->od; a.xf = s->of;
+        a.seg[0] = seg_of(L.wo, s->x, nullptr);
+        a.nseg = 1;
+        return run_gemv<IN_QUANT, EPI_RESID>(a, m->n_sm, st, count);
+    case K_W13:
+        if (is_q(L.w1) != is_q(L.w3)) return set_err("layer %d: w1 and w3 differ in quantization", l);
+        a.cols = m->dim;
+        a.x = s->x; a.norm_w = L.ffn_norm; a.eps = m->eps;
+        a.seg[0] = seg_of(L.w1, nullptr, nullptr);
+        a.seg[1] = seg_of(L.w3, nullptr, nullptr);
+        a.nseg = 2;
+        a.hq = s->hq; a.hd = s->hd; a.hf = is_q(L.w2) ? nullptr : s->hf;
+        return run_gemv<IN_NORM, EPI_SWIGLU>(a, m->n_sm, st, count);
+    case K_W2:
+        a.cols = m->hidden;
+        a.xq = s->hq; a.xd = s->hd; a.xf = s->hf;
+        a.seg[0] = seg_of(L.w2, s->x, nullptr);
+        a.nseg = 1;
+        return run_gemv<IN_QUANT, EPI_RESID>(a, m->n_sm, st, count);
+    }
+    return set_err("unknown kernel kind %d", kind);
+}
+
+static int launch_head(EmberCudaState *s, int *count) {
+    EmberCudaModel *m = s->m;
+    GemvArgs a = gemv_base(s);
+    a.cols = m->dim;
+    a.x = s->x; a.norm_w = m->final_norm; a.eps = m->eps;
+    a.seg[0] = seg_of(m->lm_head, s->logits, nullptr);
+    a.nseg = 1;
+    return run_gemv<IN_NORM, EPI_STORE>(a, m->n_sm, s->stream, count);
 }
 
 // The kernels of one token step. with_head: final norm + lm_head; tail: 0 none,
 // 1 argmax+advance (greedy), 2 advance (prefill). ids != NULL: prefill feed.
 static int record_step(EmberCudaState *s, bool with_layers, bool with_head, int tail, const int *ids, int *count) {
     EmberCudaModel *m = s->m;
-    cudaStream_t st = s->stream;
-    const int hd = m->head_dim, kvd = m->n_kv * hd;
-    const size_t es = s->kv_fp16 ? 2 : 4;
     if (with_layers) {
-        EmbedArgs ea;
-        ea.q = m->tok_emb.q; ea.s = m->tok_emb.s; ea.dtype = m->tok_emb.dtype; ea.dim = m->dim;
-        ea.ctl = s->ctl; ea.ids = ids; ea.x = s->x;
-        CK(launch_pdl(embed_kernel, 1, 256, 0, st, ea));
-        (*count)++;
-        for (int l = 0; l < m->n_layers; l++) {
-            const DevLayer &L = m->layers[l];
-            GemvArgs a;
-            memset(&a, 0, sizeof(a));
-            a.ex = m->ex;
-            a.cols = m->dim;
-            a.x = s->x; a.norm_w = L.attn_norm; a.eps = m->eps;
-            a.seg[0] = seg_of(L.wq, s->q, L.bq);
-            a.seg[1] = seg_of(L.wk, s->k, L.bk);
-            a.seg[2] = seg_of(L.wv, s->v, L.bv);
-            a.nseg = 3;
-            CK((run_gemv<IN_NORM, EPI_STORE>(a, m->n_sm, st, count)));
-
-            AttnArgs at;
-            at.q = s->q; at.k = s->k; at.v = s->v;
-            at.kc = (char *)s->kc + (size_t)l * s->ctx * kvd * es;
-            at.vc = (char *)s->vc + (size_t)l * s->ctx * kvd * es;
-            at.q_norm = L.q_norm; at.k_norm = L.k_norm;
-            at.rope = s->rope; at.ctl = s->ctl; at.att = s->att;
-            at.oq = s->oq; at.od = s->od; at.of = s->of;
-            at.nh = m->n_heads; at.nkv = m->n_kv; at.hd = hd; at.ctx = s->ctx;
-            at.neox = m->rope_neox; at.eps = m->eps; at.ex = m->ex;
-            if (s->kv_fp16) CK(launch_pdl(attn_decode_kernel<__half>, m->n_heads, ATTN_THREADS, 0, st, at));
-            else CK(launch_pdl(attn_decode_kernel<float>, m->n_heads, ATTN_THREADS, 0, st, at));
-            (*count)++;
-
-            memset(&a, 0, sizeof(a));
-            a.ex = m->ex;
-            a.cols = m->n_heads * hd;
-            a.xq = s->oq; a.xd = s->od; a.xf = s->of;
-            a.seg[0] = seg_of(L.wo, s->x, nullptr);
-            a.nseg = 1;
-            CK((run_gemv<IN_QUANT, EPI_RESID>(a, m->n_sm, st, count)));
-
-            memset(&a, 0, sizeof(a));
-            a.ex = m->ex;
-            a.cols = m->dim;
-            a.x = s->x; a.norm_w = L.ffn_norm; a.eps = m->eps;
-            a.seg[0] = seg_of(L.w1, nullptr, nullptr);
-            a.seg[1] = seg_of(L.w3, nullptr, nullptr);
-            a.nseg = 2;
-            a.hq = s->hq; a.hd = s->hd; a.hf = s->hf;
-            CK((run_gemv<IN_NORM, EPI_SWIGLU>(a, m->n_sm, st, count)));
-
-            memset(&a, 0, sizeof(a));
-            a.ex = m->ex;
-            a.cols = m->hidden;
-            a.xq = s->hq; a.xd = s->hd; a.xf = s->hf;
-            a.seg[0] = seg_of(L.w2, s->x, nullptr);
-            a.nseg = 1;
-            CK((run_gemv<IN_QUANT, EPI_RESID>(a, m->n_sm, st, count)));
-        }
+        if (launch_embed(s, ids, count)) return 1;
+        for (int l = 0; l < m->n_layers; l++)
+            for (int kind = K_QKV; kind <= K_W2; kind++)
+                if (launch_layer(s, kind, l, count)) return 1;
     }
-    if (with_head) {
-        GemvArgs a;
-        memset(&a, 0, sizeof(a));
-        a.ex = m->ex;
-        a.cols = m->dim;
-        a.x = s->x; a.norm_w = m->final_norm; a.eps = m->eps;
-        a.seg[0] = seg_of(m->lm_head, s->logits, nullptr);
-        a.nseg = 1;
-        CK((run_gemv<IN_NORM, EPI_STORE>(a, m->n_sm, st, count)));
-    }
+    if (with_head && launch_head(s, count)) return 1;
     if (tail == 1) {
         ArgmaxArgs aa;
         aa.logits = s->logits; aa.n = m->vocab; aa.part_v = s->am_v; aa.part_i = s->am_i;
         aa.ticket = s->am_ticket; aa.ctl = s->ctl; aa.out = s->out_tokens;
-        CK(launch_pdl(argmax_advance_kernel, s->am_blocks, 256, 0, st, aa));
+        CK(launch_pdl(argmax_advance_kernel, s->am_blocks, 256, 0, s->stream, aa));
         (*count)++;
     } else if (tail == 2) {
-        CK(launch_pdl(advance_kernel, 1, 32, 0, st, s->ctl));
+        CK(launch_pdl(advance_kernel, 1, 32, 0, s->stream, s->ctl));
         (*count)++;
     }
     return 0;
+}
+
+// bytes a kernel of one kind must move per launch (weights, activations in and
+// out; attention: the cache of positions 0..pos plus this position's writes)
+static double mat_bytes(const DevMat &d) {
+    double rb = (double)qrow_bytes(d.dtype, d.cols);
+    double sb = d.dtype == EMBER_DT_F32 ? 0.0 : (double)(d.cols / 32) * 2.0;
+    return (double)d.rows * (rb + sb);
+}
+
+static double kernel_bytes(const EmberCudaState *s, int kind, int l, int pos) {
+    const EmberCudaModel *m = s->m;
+    const int hd = m->head_dim, qd = m->n_heads * hd, kvd = m->n_kv * hd;
+    const double es = s->kv_fp16 ? 2.0 : 4.0;
+    const DevLayer &L = m->layers[l];
+    switch (kind) {
+    case K_QKV: return mat_bytes(L.wq) + mat_bytes(L.wk) + mat_bytes(L.wv) + 8.0 * m->dim + 4.0 * (qd + 2 * kvd);
+    case K_ATTN: return 2.0 * kvd * es * (pos + 1) + 4.0 * (qd + 2 * kvd) + qd + qd / 32 * 4.0;
+    case K_WO: return mat_bytes(L.wo) + qd + qd / 32 * 4.0 + 8.0 * m->dim;
+    case K_W13: return mat_bytes(L.w1) + mat_bytes(L.w3) + 8.0 * m->dim + m->hidden + m->hidden / 32 * 4.0;
+    case K_W2: return mat_bytes(L.w2) + m->hidden + m->hidden / 32 * 4.0 + 8.0 * m->dim;
+    case K_HEAD: return mat_bytes(m->lm_head) + 8.0 * m->dim + 4.0 * m->vocab;
+    }
+    return 0.0;
 }
 
 static int record_kind(EmberCudaState *s, int kind) {
@@ -493,6 +617,7 @@ static int record_kind(EmberCudaState *s, int kind) {
         CK(cudaMemcpyAsync(s->ctl, s->h_ctl, 2 * sizeof(int), cudaMemcpyHostToDevice, st));
         if (record_step(s, true, true, 0, nullptr, &count)) return 1;
         CK(cudaMemcpyAsync(s->h_logits, s->logits, (size_t)s->m->vocab * 4, cudaMemcpyDeviceToHost, st));
+        CK(cudaMemcpyAsync(s->h_ctl + CTL_ERR, s->ctl + CTL_ERR, sizeof(int), cudaMemcpyDeviceToHost, st));
         s->launches_per_step = count;
     } else if (kind == 1) {
         if (record_step(s, true, true, 1, nullptr, &count)) return 1;
@@ -524,15 +649,34 @@ static int capture(EmberCudaState *s, cudaGraphExec_t *exec, int kind) {
     return 0;
 }
 
+// a bounded device wait gave up: report it (the step's results are invalid)
+static int check_device_error(EmberCudaState *s, int err) {
+    if (err == ERR_NONE) return 0;
+    cudaMemsetAsync(s->ctl + CTL_ERR, 0, sizeof(int), s->stream);
+    cudaStreamSynchronize(s->stream);
+    return set_err("device wait timed out (code %d): a bulk copy never completed", err);
+}
+
 extern "C" int ember_cuda_forward(EmberCudaState *s, int tok, int pos, float *host_logits) {
     CK(cudaSetDevice(s->m->device));
     if (!s->g_fwd && capture(s, &s->g_fwd, 0)) return 1;
     s->h_ctl[CTL_POS] = pos;
     s->h_ctl[CTL_TOK] = tok;
+    s->h_ctl[CTL_ERR] = 0;
     CK(cudaGraphLaunch(s->g_fwd, s->stream));
     CK(cudaStreamSynchronize(s->stream));
+    if (check_device_error(s, s->h_ctl[CTL_ERR])) return 1;
     if (host_logits && host_logits != s->h_logits) memcpy(host_logits, s->h_logits, (size_t)s->m->vocab * 4);
     return 0;
+}
+
+static int read_error_word(EmberCudaState *s) {
+    int err = 0;
+    if (cudaMemcpyAsync(&s->h_ctl[CTL_ERR], s->ctl + CTL_ERR, sizeof(int), cudaMemcpyDeviceToHost, s->stream) != cudaSuccess ||
+        cudaStreamSynchronize(s->stream) != cudaSuccess)
+        return set_err("reading the device error word failed");
+    err = s->h_ctl[CTL_ERR];
+    return check_device_error(s, err);
 }
 
 extern "C" int ember_cuda_prefill(EmberCudaState *s, const int *ids, int n, int start, float *host_logits) {
@@ -540,12 +684,15 @@ extern "C" int ember_cuda_prefill(EmberCudaState *s, const int *ids, int n, int 
     if (n <= 0) return 0;
     if (!s->g_prefill && capture(s, &s->g_prefill, 2)) return 1;
     if (!s->g_head && capture(s, &s->g_head, 3)) return 1;
-    int ctl[CTL_WORDS] = { start, 0, 0, start };
+    int *hc = s->h_ctl;
+    CK(cudaStreamSynchronize(s->stream));
+    hc[CTL_POS] = start; hc[CTL_TOK] = 0; hc[CTL_NOUT] = 0; hc[CTL_BASE] = start; hc[CTL_ERR] = 0;
     CK(cudaMemcpyAsync(s->ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, s->stream));
-    CK(cudaMemcpyAsync(s->ctl, ctl, sizeof(ctl), cudaMemcpyHostToDevice, s->stream));
+    CK(cudaMemcpyAsync(s->ctl, hc, 5 * sizeof(int), cudaMemcpyHostToDevice, s->stream));
     for (int i = 0; i < n; i++) CK(cudaGraphLaunch(s->g_prefill, s->stream));
     CK(cudaGraphLaunch(s->g_head, s->stream));
     CK(cudaStreamSynchronize(s->stream));
+    if (read_error_word(s)) return 1;
     if (host_logits && host_logits != s->h_logits) memcpy(host_logits, s->h_logits, (size_t)s->m->vocab * 4);
     return 0;
 }
@@ -555,13 +702,104 @@ extern "C" int ember_cuda_greedy(EmberCudaState *s, int tok, int pos, int n_step
     CK(cudaSetDevice(s->m->device));
     if (n_steps <= 0) return 0;
     if (!s->g_greedy && capture(s, &s->g_greedy, 1)) return 1;
-    int ctl[CTL_WORDS] = { pos, tok, 0, 0 };
-    CK(cudaMemcpyAsync(s->ctl, ctl, sizeof(ctl), cudaMemcpyHostToDevice, s->stream));
+    int *hc = s->h_ctl;
+    CK(cudaStreamSynchronize(s->stream));
+    hc[CTL_POS] = pos; hc[CTL_TOK] = tok; hc[CTL_NOUT] = 0; hc[CTL_BASE] = 0; hc[CTL_ERR] = 0;
+    CK(cudaMemcpyAsync(s->ctl, hc, 5 * sizeof(int), cudaMemcpyHostToDevice, s->stream));
     for (int i = 0; i < n_steps; i++) CK(cudaGraphLaunch(s->g_greedy, s->stream));
     if (host_tokens) CK(cudaMemcpyAsync(host_tokens, s->out_tokens, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, s->stream));
     if (host_logits) CK(cudaMemcpyAsync(host_logits, s->logits, (size_t)s->m->vocab * 4, cudaMemcpyDeviceToHost, s->stream));
     CK(cudaStreamSynchronize(s->stream));
+    return read_error_word(s);
+}
+
+extern "C" int ember_cuda_profile_step(EmberCudaState *s, int tok, int pos, float *ms_out, int cap,
+                                       int *n_out) {
+    CK(cudaSetDevice(s->m->device));
+    *n_out = 0;
+    std::vector<cudaEvent_t> ev((size_t)cap + 1, nullptr);
+    for (auto &e : ev) CK(cudaEventCreate(&e));
+    int *hc = s->h_ctl;
+    CK(cudaStreamSynchronize(s->stream));
+    hc[CTL_POS] = pos; hc[CTL_TOK] = tok; hc[CTL_NOUT] = 0; hc[CTL_BASE] = 0; hc[CTL_ERR] = 0;
+    int rc = cudaMemcpyAsync(s->ctl, hc, 5 * sizeof(int), cudaMemcpyHostToDevice, s->stream) != cudaSuccess;
+    g_prof_events = ev.data();
+    g_prof_n = 0;
+    g_prof_cap = cap;
+    int count = 0;
+    if (!rc) rc = record_step(s, true, true, 1, nullptr, &count);
+    const int n = g_prof_n;
+    g_prof_events = nullptr;
+    if (!rc && cudaEventRecord(ev[n], s->stream) != cudaSuccess) rc = 1;
+    if (!rc && cudaStreamSynchronize(s->stream) != cudaSuccess) rc = 1;
+    for (int i = 0; i < n && !rc; i++) {
+        float ms = 0;
+        if (cudaEventElapsedTime(&ms, ev[i], ev[i + 1]) != cudaSuccess) rc = 1;
+        ms_out[i] = ms;
+    }
+    for (auto &e : ev) cudaEventDestroy(e);
+    if (rc) return set_err("profile step failed: %s", cudaGetErrorString(cudaGetLastError()));
+    *n_out = n;
+    return read_error_word(s);
+}
+
+// ---- timing hooks (CUDA events on the state's stream) ----
+
+static cudaEvent_t g_marks[8];
+static int g_marks_ready = 0;
+
+extern "C" int ember_cuda_mark(EmberCudaState *s, int slot) {
+    if (slot < 0 || slot >= 8) return set_err("mark slot %d out of range", slot);
+    CK(cudaSetDevice(s->m->device));
+    if (!g_marks_ready) {
+        for (int i = 0; i < 8; i++) CK(cudaEventCreate(&g_marks[i]));
+        g_marks_ready = 1;
+    }
+    CK(cudaEventRecord(g_marks[slot], s->stream));
     return 0;
+}
+
+extern "C" int ember_cuda_elapsed_ms(EmberCudaState *s, int a, int b, float *ms) {
+    if (!g_marks_ready || a < 0 || a >= 8 || b < 0 || b >= 8) return set_err("bad mark slots");
+    CK(cudaSetDevice(s->m->device));
+    CK(cudaEventSynchronize(g_marks[b]));
+    CK(cudaEventElapsedTime(ms, g_marks[a], g_marks[b]));
+    return 0;
+}
+
+// Times `reps` rounds of one kernel kind launched for every layer in turn (so
+// each launch reads weights that are not in L2), outside any graph, on the
+// state's stream between two events. Reports the mean device time per launch
+// and the algorithmic bytes per launch (mean over layers, attention at the
+// state's current position). The launches change the state's activations and
+// cache, so the state is only good for timing afterwards.
+extern "C" int ember_cuda_time_kernel(EmberCudaState *s, int kind, int reps, float *ms_per_launch,
+                                      double *bytes_per_launch) {
+    CK(cudaSetDevice(s->m->device));
+    if (kind < K_QKV || kind > K_HEAD || reps <= 0) return set_err("bad kernel kind / reps");
+    int hc[CTL_WORDS];
+    CK(cudaMemcpy(hc, s->ctl, sizeof(hc), cudaMemcpyDeviceToHost));
+    const int L = kind == K_HEAD ? 1 : s->m->n_layers;
+    double bytes = 0;
+    for (int l = 0; l < L; l++) bytes += kernel_bytes(s, kind, kind == K_HEAD ? 0 : l, hc[CTL_POS]);
+    *bytes_per_launch = bytes / L;
+    cudaEvent_t e0, e1;
+    CK(cudaEventCreate(&e0));
+    CK(cudaEventCreate(&e1));
+    int count = 0, rc = 0;
+    // one untimed round first
+    for (int l = 0; l < L && !rc; l++) rc = kind == K_HEAD ? launch_head(s, &count) : launch_layer(s, kind, l, &count);
+    if (!rc && cudaEventRecord(e0, s->stream) != cudaSuccess) rc = 1;
+    for (int r = 0; r < reps && !rc; r++)
+        for (int l = 0; l < L && !rc; l++) rc = kind == K_HEAD ? launch_head(s, &count) : launch_layer(s, kind, l, &count);
+    if (!rc && cudaEventRecord(e1, s->stream) != cudaSuccess) rc = 1;
+    float ms = 0;
+    if (!rc && (cudaEventSynchronize(e1) != cudaSuccess || cudaEventElapsedTime(&ms, e0, e1) != cudaSuccess)) rc = 1;
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (rc) return set_err("kernel timing failed: %s", cudaGetErrorString(cudaGetLastError()));
+    *ms_per_launch = ms / (float)(reps * L);
+    return read_error_word(s);
 }
 
 // ------------------------------------------------------------- op level -------
@@ -582,9 +820,12 @@ static int op_matmul(float *out, const float *x, const void *w, int dtype, int n
     int rc = upload_mat(&tmp, &dm, hm);
     float *dx = nullptr, *dout = nullptr, *dxd = nullptr;
     int8_t *dxq = nullptr;
+    int *derr = nullptr;
     const int nb = n_in / 32;
     if (!rc) rc = dalloc(&tmp, (void **)&dx, (size_t)n_in * 4) || dalloc(&tmp, (void **)&dout, (size_t)d_out * 4) ||
-                  dalloc(&tmp, (void **)&dxq, (size_t)n_in + 16) || dalloc(&tmp, (void **)&dxd, (size_t)nb * 4 + 4);
+                  dalloc(&tmp, (void **)&dxq, (size_t)n_in + 16) || dalloc(&tmp, (void **)&dxd, (size_t)nb * 4 + 16) ||
+                  dalloc(&tmp, (void **)&derr, 16);
+    if (!rc && cudaMemset(derr, 0, 16) != cudaSuccess) rc = set_err("memset");
     std::vector<int8_t> hq(n_in + 16);
     std::vector<float> hd(nb + 1);
     int nsm = 148;
@@ -597,11 +838,14 @@ static int op_matmul(float *out, const float *x, const void *w, int dtype, int n
         a.x = dx;
         a.xq_out = dxq;
         a.xd_out = dxd;
+        a.err = derr;
         a.seg[0] = seg_of(dm, dout, nullptr);
         a.nseg = 1;
-        cudaError_t e = run_gemv<IN_RAW, EPI_STORE>(a, nsm, 0, nullptr);
-        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (run_gemv<IN_RAW, EPI_STORE>(a, nsm, 0, nullptr)) { rc = 1; break; }
+        cudaError_t e = cudaDeviceSynchronize();
         if (e != cudaSuccess) { rc = set_err("ember_matmul kernel: %s", cudaGetErrorString(e)); break; }
+        int herr = 0;
+        if (cudaMemcpy(&herr, derr, 4, cudaMemcpyDeviceToHost) != cudaSuccess || herr) { rc = set_err("ember_matmul: device wait timed out"); break; }
         if (cudaMemcpy(out + (size_t)b * d_out, dout, (size_t)d_out * 4, cudaMemcpyDeviceToHost) != cudaSuccess) { rc = set_err("copy"); break; }
         if (dtype != EMBER_DT_F32 && xq) {
             if (cudaMemcpy(hq.data(), dxq, (size_t)n_in, cudaMemcpyDeviceToHost) != cudaSuccess ||

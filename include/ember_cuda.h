@@ -95,6 +95,22 @@ int  ember_cuda_prefill(EmberCudaState *s, const int *ids, int n, int start, flo
 int  ember_cuda_greedy(EmberCudaState *s, int tok, int pos, int n_steps, int *host_tokens,
                        float *host_logits);
 
+/* Profiling: runs one complete greedy step (token `tok` at `pos`, every kernel
+ * of the step, no graph, no programmatic overlap) with a CUDA event before each
+ * launch, and writes each launch's device time in ms to ms_out[0..*n_out). */
+int  ember_cuda_profile_step(EmberCudaState *s, int tok, int pos, float *ms_out, int cap, int *n_out);
+
+/* Device timing on the state's stream: record event `slot` (0..7), and the time
+ * in ms between two recorded slots (waits for the later one). */
+int  ember_cuda_mark(EmberCudaState *s, int slot);
+int  ember_cuda_elapsed_ms(EmberCudaState *s, int a, int b, float *ms);
+/* Mean device time of one kernel kind (0 qkv, 1 attention, 2 wo, 3 w1/w3+SwiGLU,
+ * 4 w2, 5 lm_head), launched `reps` times for every layer in turn outside any
+ * graph, and its algorithmic bytes per launch. Leaves the state usable only for
+ * further timing (activations and cache are overwritten). */
+int  ember_cuda_time_kernel(EmberCudaState *s, int kind, int reps, float *ms_per_launch,
+                            double *bytes_per_launch);
+
 /* the state's pinned host logits buffer (vocab floats), owned by the state */
 float       *ember_cuda_state_host_logits(EmberCudaState *s);
 
