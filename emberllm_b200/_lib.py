@@ -61,7 +61,8 @@ CUDA_SYMBOLS = [
     "ember_cuda_greedy", "ember_cuda_state_host_logits", "ember_cuda_state_stream",
     "ember_cuda_state_logits_dev", "ember_cuda_state_launches_per_step", "ember_cuda_error",
     "ember_cuda_available", "ember_cuda_profile_step", "ember_cuda_mark", "ember_cuda_elapsed_ms",
-    "ember_cuda_time_kernel", "ember_host_expf_params", "ember_host_expf_emulated",
+    "ember_cuda_time_kernel", "ember_cuda_argmax_static", "ember_host_expf_params",
+    "ember_host_expf_emulated",
     "ember_host_rope_table", "ember_forward_greedy", "ember_state_cuda",
 ]
 

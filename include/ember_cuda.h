@@ -111,6 +111,19 @@ int  ember_cuda_elapsed_ms(EmberCudaState *s, int a, int b, float *ms);
 int  ember_cuda_time_kernel(EmberCudaState *s, int kind, int reps, float *ms_per_launch,
                             double *bytes_per_launch);
 
+/* Greedy pick without allocating: the first index of the largest of n device
+ * floats `logits`, written to the device int `out_index`, enqueued on `stream`
+ * (a cudaStream_t; NULL is the default stream). No counterpart in the reference.
+ * For callers that cannot let the library allocate device memory (a host that
+ * owns the GPU's memory through its own pool, or a per-token path that must not
+ * risk cudaMalloc's synchronisation): it takes only caller-owned buffers and
+ * keeps its scratch in a fixed array inside the library (about 2 KB per device,
+ * held until exit). n must be in [1, 67108864]; other sizes are rejected with
+ * status 1 and a line on stderr (2: bad pointer, 3: CUDA error). The first call
+ * on a device looks the array up and should come before any stream capture;
+ * calls that overlap on the GPU share the array and race. */
+int  ember_cuda_argmax_static(const float *logits, int n, int *out_index, void *stream);
+
 /* the state's pinned host logits buffer (vocab floats), owned by the state */
 float       *ember_cuda_state_host_logits(EmberCudaState *s);
 
