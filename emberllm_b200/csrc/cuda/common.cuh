@@ -63,6 +63,28 @@ EMB_DEV int8_t quant_lane(float x, float *dq) {
     return (int8_t)(int)q;
 }
 
+// Quantize four consecutive elements of a 32-block whose eight quads sit in
+// eight consecutive lanes (lanes of one block all active, in `mask`): the same
+// arithmetic as quant_lane, the block max reduced over the eight lanes. Returns
+// the four int8 codes packed little-endian.
+EMB_DEV uint32_t quant_quad(float4 v, unsigned mask, float *dq) {
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    amax = fmaxf(amax, __shfl_xor_sync(mask, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(mask, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(mask, amax, 4));
+    const float d = fdiv(amax, 127.0f);
+    const float id = d > 0.0f ? fdiv(1.0f, d) : 0.0f;
+    *dq = __half2float(__float2half_rn(d));
+    float q[4] = {v.x, v.y, v.z, v.w};
+    uint32_t packed = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        float t = fminf(fmaxf(round_half_away(fmul(q[j], id)), -127.0f), 127.0f);
+        packed |= (uint32_t)(uint8_t)(int8_t)(int)t << (8 * j);
+    }
+    return packed;
+}
+
 // Bytes of one row in the device layout: Q8_0 32 int8 per block, Q4_0 16 bytes
 // per block, fp32 4 bytes per element.
 __host__ __device__ inline size_t qrow_bytes(int dtype, int cols) {
@@ -84,10 +106,44 @@ __host__ __device__ inline size_t qrow_bytes(int dtype, int cols) {
 // position word), and must not read what its immediate predecessor writes.
 EMB_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 EMB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ---- optional phase probes ----------------------------------------------------
+// Built only with -DEMBER_PROBES (a separate profiling build): CTA 0 records the
+// global timer at named phase boundaries of each kernel kind (the last launch of
+// each kind wins), and every launch records when it reached and left its
+// dependency wait. They record timestamps only and change no computation.
+#ifdef EMBER_PROBES
+__device__ unsigned long long g_probe[8][16];
+__device__ unsigned g_wait_count;
+__device__ unsigned long long g_wait_times[8192][2];
+EMB_DEV unsigned long long probe_now() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+#define EMB_PROBE(kind, slot)                                                     \
+    do {                                                                          \
+        if (blockIdx.x == 0 && threadIdx.x == 0) g_probe[kind][slot] = probe_now(); \
+    } while (0)
+EMB_DEV void pdl_wait_then_release() {
+    unsigned long long t0 = probe_now();
+    pdl_wait();
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        unsigned id = atomicAdd(&g_wait_count, 1u) & 8191u;
+        g_wait_times[id][0] = t0;
+        g_wait_times[id][1] = probe_now();
+    }
+    pdl_launch_dependents();
+}
+#else
+#define EMB_PROBE(kind, slot) \
+    do {                      \
+    } while (0)
 EMB_DEV void pdl_wait_then_release() {
     pdl_wait();
     pdl_launch_dependents();
 }
+#endif
 
 // ---- exact sequential sums ---------------------------------------------------
 // sum = ((0 + v[0]) + v[1]) + ... in index order: the reference's loop. The

@@ -26,6 +26,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "exact_sum.cuh"
 
 namespace emb {
 
@@ -86,16 +87,23 @@ __host__ __device__ inline size_t gemv_sub_bytes(int dtype, int rows, int cols) 
     return pad16((size_t)rows * qrow_bytes(dtype, cols)) + pad16((size_t)rows * (cols / 32) * 2);
 }
 
+// bytes of the region that holds the tile products P, and during an RMSNorm
+// prologue (before any tile) the norm weights, the squares and the exact-sum
+// scratch instead
+__host__ __device__ inline size_t gemv_p_bytes(int cols, bool in_norm) {
+    size_t p = (size_t)2 * GEMV_MAX_ROWS * gemv_p_stride(cols / 32) * 4;
+    size_t pro = in_norm ? (size_t)cols * 8 + sizeof(XsScratch) : (size_t)cols * 4;
+    return pad16(p > pro ? p : pro);
+}
+
 // dynamic shared memory of gemv_kernel
-__host__ inline size_t gemv_smem_bytes(const GemvArgs &a, bool need_xf) {
+__host__ inline size_t gemv_smem_bytes(const GemvArgs &a, bool need_xf, bool in_norm) {
     const int cols = a.cols, nb = cols / 32;
     size_t b = a.quantized ? (size_t)a.stages * a.stage_bytes : 0;
     b += pad16(cols);                                           // xq
     b += pad16((size_t)(nb > 0 ? nb : 1) * 4);                  // xd
     if (need_xf) b += (size_t)cols * 4;                         // xf
-    size_t p = (size_t)2 * GEMV_MAX_ROWS * gemv_p_stride(nb) * 4;
-    size_t sq = (size_t)cols * 4;
-    b += p > sq ? p : sq;                                       // P (also sq scratch)
+    b += gemv_p_bytes(cols, in_norm);                           // P / prologue scratch
     b += 2 * GEMV_MAX_ROWS * 4;                                 // row sums
     return b;
 }
@@ -211,10 +219,13 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
     float *xf_s = reinterpret_cast<float *>(smem + off);
     if (need_xf) off += (size_t)cols * 4;
     float *P = reinterpret_cast<float *>(smem + off);
-    size_t psz = (size_t)2 * GEMV_MAX_ROWS * pstride * 4, sqsz = (size_t)cols * 4;
-    off += psz > sqsz ? psz : sqsz;
+    off += gemv_p_bytes(cols, IN == IN_NORM);
     float *rowsum = reinterpret_cast<float *>(smem + off);
 
+    // probe kind: 0 q/k/v, 5 lm_head, 1 w1/w3, 2 wo/w2, 3 op-level
+    const int PK = IN == IN_NORM ? (EPI == EPI_SWIGLU ? 1 : (a.nseg == 1 ? 5 : 0)) : (IN == IN_QUANT ? 2 : 3);
+    EMB_PROBE(PK, 0);
+    (void)PK;
     // ---- pre-wait: only weights (the tiles and the norm vector) ----
     if (S > 0 && tid == 0) {
         for (int s = 0; s < S; s++) mbar_init(&bars[s], 1);
@@ -222,10 +233,15 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
         for (int k = 0; k < S && k < my_tiles; k++)
             issue_tile<EPI>(a, blockIdx.x + k * gridDim.x, stage0 + (size_t)k * a.stage_bytes, &bars[k]);
     }
-    float *nw_s = P;   // the norm weights live in P until the tiles need it
+    // until the tiles need P: the norm weights, the squares, the exact-sum scratch
+    float *nw_s = P;
+    float *sq_s = P + cols;
+    XsScratch *xs = reinterpret_cast<XsScratch *>(P + 2 * (size_t)cols);
     if (IN == IN_NORM)
         for (int i = tid; i < cols; i += GEMV_THREADS) nw_s[i] = a.norm_w[i];
+    EMB_PROBE(PK, 1);
     pdl_wait_then_release();
+    EMB_PROBE(PK, 2);
 
     // ---- prologue: the Q8_0 activation (and fp32 copy) in shared memory ----
     if (IN == IN_QUANT) {
@@ -240,27 +256,38 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
             // RMSNorm (ref src/model.c:50-55): the sum of squares as ONE sequential
             // chain in index order, as the reference adds
             __syncthreads();
+            EMB_PROBE(PK, 3);
             if (tid == 0) s_scale = rms_scale(chain_sumsq(xf_s, cols), cols, a.eps);
             __syncthreads();
+            EMB_PROBE(PK, 4);
+            (void)sq_s;
+            (void)xs;
             const float sc = s_scale;
             for (int i = tid; i < cols; i += GEMV_THREADS)
                 xf_s[i] = fmul(fmul(xf_s[i], sc), nw_s[i]);   // (x*scale)*w
         }
         __syncthreads();
-        // quantize the activation, one warp per 32-block (ref src/kernels.c:211)
-        const int warp = tid >> 5, lane = tid & 31;
-        for (int b = warp; b < nb; b += GEMV_THREADS / 32) {
-            float dq;
-            int8_t q = quant_lane(xf_s[b * 32 + lane], &dq);
-            xq_s[b * 32 + lane] = q;
-            if (lane == 0) xd_s[b] = dq;
-            if (IN == IN_RAW && blockIdx.x == 0 && a.xq_out) {
-                a.xq_out[b * 32 + lane] = q;
-                if (lane == 0) a.xd_out[b] = dq;
+        // quantize the activation (ref src/kernels.c:211): eight threads per
+        // 32-block, four elements each, every block at once
+        for (int base = 0; base < nb * 8; base += GEMV_THREADS) {
+            const int q8 = base + tid;
+            const bool act = q8 < nb * 8;
+            const unsigned mask = __ballot_sync(0xffffffffu, act);
+            if (act) {
+                const int b = q8 >> 3, sub = q8 & 7;
+                float dq;
+                const uint32_t packed = quant_quad(reinterpret_cast<const float4 *>(xf_s + b * 32)[sub], mask, &dq);
+                reinterpret_cast<uint32_t *>(xq_s + b * 32)[sub] = packed;
+                if (sub == 0) xd_s[b] = dq;
+                if (IN == IN_RAW && blockIdx.x == 0 && a.xq_out) {
+                    reinterpret_cast<uint32_t *>(a.xq_out + b * 32)[sub] = packed;
+                    if (sub == 0) a.xd_out[b] = dq;
+                }
             }
         }
     }
     __syncthreads();
+    EMB_PROBE(PK, 5);
 
     // ---- tiles ----
     for (int k = 0; k < my_tiles; k++) {
@@ -274,6 +301,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
             const int st = k % S;
             const unsigned char *stage = stage0 + (size_t)st * a.stage_bytes;
             mbar_wait_cta(&bars[st], (uint32_t)((k / S) & 1), a.err, ERR_GEMV_WAIT);
+            if (k == 0) EMB_PROBE(PK, 6);
             // phase 1: per (row, block) terms ((float)acc * d_w) * d_x into P
             size_t soff = 0;
 #pragma unroll
@@ -300,6 +328,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
                 soff += gemv_sub_bytes(g.dtype, R, cols);
             }
             __syncthreads();
+            if (k == 0) EMB_PROBE(PK, 7);
             // the stage is free: refill it with this CTA's tile k + S
             if (tid == 0 && k + S < my_tiles) {
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -327,6 +356,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
             }
         }
         __syncthreads();
+        if (k == 0) EMB_PROBE(PK, 8);
         // epilogue
         const int row0 = tr[0].row0;
         if (EPI == EPI_SWIGLU) {
@@ -356,7 +386,9 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
             }
         }
         __syncthreads();
+        if (k == 0) EMB_PROBE(PK, 9);
     }
+    EMB_PROBE(PK, 10);
 }
 
 // ---------------------------------------------------------------- attention ----
@@ -434,6 +466,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
     __shared__ float2 cs_s[128];
     __shared__ float red[ATTN_THREADS / 32];
     __shared__ float s_q, s_k, s_max, s_inv;
+    __shared__ XsScratch xs;
     const int h = blockIdx.x, tid = threadIdx.x, hd = a.hd, CH = a.chunk;
     const int kv_mul = a.nh / a.nkv, kvh = h / kv_mul;
     const int warp = tid >> 5, lane = tid & 31;
@@ -444,6 +477,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
                                : a.att + (size_t)h * a.ctx;
     int *err = a.ctl + CTL_ERR;
     uint32_t ph0 = 0, ph1 = 0;
+    EMB_PROBE(4, 0);
 
     // ---- pre-wait ----
     if (tid == 0) {
@@ -467,7 +501,9 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
         bulk_g2s(buf1, vt, (uint32_t)(n0 * hd * sizeof(T)), &bars[1]);
     }
     if (n0 > 0) load_k_chunk(buf0, kt, a.kstride, 0, n0, hd, CH);   // keys of chunk 0 -> buf0
+    EMB_PROBE(4, 1);
     pdl_wait_then_release();
+    EMB_PROBE(4, 2);
 
     // ---- this position: q, k, v; QK-norm; RoPE; KV store ----
     if (tid < hd) {
@@ -476,6 +512,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
         vs[tid] = a.v[kvh * hd + tid];
     }
     __syncthreads();
+    EMB_PROBE(4, 3);
     if (a.q_norm) {
         // per-head RMSNorm of q and k, in place (ref src/model.c:386-389); the two
         // sequential sums run on different warps
@@ -488,6 +525,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
         }
         __syncthreads();
     }
+    EMB_PROBE(4, 4);
     // RoPE (ref src/model.c:66-80) with the host-built cos/sin table
     if (tid < hd / 2) {
         const int ia = a.neox ? tid : 2 * tid, ib = a.neox ? tid + hd / 2 : 2 * tid + 1;
@@ -515,6 +553,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
     }
     __syncthreads();
 
+    EMB_PROBE(4, 5);
     // ---- scores: sc = sum_i q_i*k_i in index order, then * (1/sqrt(hd)) ----
     const float inv_sqrt = fdiv(1.0f, fsqrt((float)hd));
     for (int c = 0; c < nchunks; c++) {
@@ -536,12 +575,16 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
             att[c0 + t] = fmul(sc, inv_sqrt);
         }
     }
-    if (tid == 0) {
+    // the score at t == pos (keys in registers' smem copy), on a thread that had
+    // no position in the last chunk
+    const int last_n = nchunks > 0 ? pos - (nchunks - 1) * CH : 0;
+    if (tid == last_n % ATTN_THREADS) {
         float sc = 0.0f;
         for (int i = 0; i < hd; i++) sc = fadd(sc, fmul(qs[i], ks[i]));
         att[pos] = fmul(sc, inv_sqrt);
     }
     __syncthreads();
+    EMB_PROBE(4, 6);
     // the keys are done: value chunk 1 may stream into buf0 during the softmax
     if (tid == 0 && nchunks > 1) {
         const int n1 = min(CH, pos - CH);
@@ -565,12 +608,20 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
     const float mx = s_max;
     for (int t = tid; t <= pos; t += ATTN_THREADS) att[t] = expf_exact(a.ex, fsub(att[t], mx));
     __syncthreads();
-    if (tid == 0) s_inv = fdiv(1.0f, chain_sum(0.0f, att, pos + 1));   // sequential, t = 0..pos
+    // the denominator: the reference's sequential sum over t = 0..pos; long
+    // sums use the CTA-parallel exact evaluation
+    if (pos + 1 > 2048) {
+        const float den = exact_pos_sum<ATTN_THREADS>(att, pos + 1, &xs);
+        if (tid == 0) s_inv = fdiv(1.0f, den);
+    } else if (tid == 0) {
+        s_inv = fdiv(1.0f, chain_sum(0.0f, att, pos + 1));
+    }
     __syncthreads();
     const float inv = s_inv;
     for (int t = tid; t <= pos; t += ATTN_THREADS) att[t] = fmul(att[t], inv);
     __syncthreads();
 
+    EMB_PROBE(4, 7);
     // ---- out_i = sum_t w_t * v_t,i, sequential over t (ref src/model.c:252-256) ----
     float o = 0.0f;
     for (int c = 0; c < nchunks; c++) {
@@ -600,6 +651,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
             bulk_g2s(vb, vt + (size_t)(c + 2) * CH * hd, (uint32_t)(n2 * hd * sizeof(T)), bb);
         }
     }
+    EMB_PROBE(4, 8);
     if (tid < hd) {
         o = fadd(o, fmul(att[pos], vs[tid]));
         const int gi = h * hd + tid;
@@ -609,6 +661,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
         a.oq[gi] = q;
         if (lane == 0) a.od[gi / 32] = dq;
     }
+    EMB_PROBE(4, 9);
 }
 
 // ---------------------------------------------------------------- embedding ----

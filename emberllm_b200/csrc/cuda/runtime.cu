@@ -78,16 +78,24 @@ extern "C" int ember_cuda_available(void) {
 
 // Raise the dynamic shared-memory limit of every kernel instantiation once per
 // device, outside any stream capture.
+// each kernel may use the device's opt-in maximum minus its own static smem
+template <typename K>
+static int allow_max_smem(K kernel, int optin) {
+    cudaFuncAttributes fa;
+    CK(cudaFuncGetAttributes(&fa, kernel));
+    CK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes));
+    return 0;
+}
+
 static int init_kernel_attrs(int device) {
     static unsigned done_mask = 0;
     if (device < 32 && ((done_mask >> device) & 1u)) return 0;
-    const int lim = 220 * 1024;
-    CK(cudaFuncSetAttribute(gemv_kernel<IN_RAW, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
-    CK(cudaFuncSetAttribute(gemv_kernel<IN_NORM, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
-    CK(cudaFuncSetAttribute(gemv_kernel<IN_NORM, EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
-    CK(cudaFuncSetAttribute(gemv_kernel<IN_QUANT, EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
-    CK(cudaFuncSetAttribute(attn_decode_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
-    CK(cudaFuncSetAttribute(attn_decode_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+    int optin = 0;
+    CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+    if (allow_max_smem(gemv_kernel<IN_RAW, EPI_STORE>, optin) || allow_max_smem(gemv_kernel<IN_NORM, EPI_STORE>, optin) ||
+        allow_max_smem(gemv_kernel<IN_NORM, EPI_SWIGLU>, optin) || allow_max_smem(gemv_kernel<IN_QUANT, EPI_RESID>, optin) ||
+        allow_max_smem(attn_decode_kernel<float>, optin) || allow_max_smem(attn_decode_kernel<__half>, optin))
+        return 1;
     if (device < 32) done_mask |= 1u << device;
     return 0;
 }
@@ -208,11 +216,15 @@ extern "C" int ember_cuda_model_upload(const EmberCudaModelDesc *d, const EmberE
              upload_vec(m, &L.bv, d->b_v[l], kvd);
     }
     if (!rc) {
+        // the expf recipe's 2^(j/64) table, then the exception slots
         m->ex.p = *e;
+        double *tab = nullptr;
         uint32_t *slots = nullptr;
-        rc = dalloc(m, (void **)&slots, (size_t)e->n_slots * 8);
-        if (!rc && cudaMemcpy(slots, e->slots, (size_t)e->n_slots * 8, cudaMemcpyHostToDevice) != cudaSuccess)
+        rc = dalloc(m, (void **)&tab, 64 * sizeof(double)) || dalloc(m, (void **)&slots, (size_t)e->n_slots * 8);
+        if (!rc && (cudaMemcpy(tab, e->tab, 64 * sizeof(double), cudaMemcpyHostToDevice) != cudaSuccess ||
+                    cudaMemcpy(slots, e->slots, (size_t)e->n_slots * 8, cudaMemcpyHostToDevice) != cudaSuccess))
             rc = set_err("expf table upload failed");
+        m->ex.p.tab = tab;
         m->ex.p.slots = slots;
     }
     if (rc) { model_release(m); delete m; return 1; }
@@ -439,20 +451,39 @@ static int run_gemv(GemvArgs a, int n_sm, cudaStream_t st, int *count) {
     size_t sb = 0;
     for (int sub = 0; sub < nsub; sub++) sb += gemv_sub_bytes(a.seg[sub].dtype, R, a.cols);
     a.stage_bytes = (int)((sb + 127) / 128 * 128);
-    // one CTA per tile for layer-sized matrices; a persistent ring for lm_head
-    int grid = total;
-    if (grid > 2 * n_sm) grid = 2 * n_sm;
-    if (grid < 1) grid = 1;
-    const int per_cta = (total + grid - 1) / grid;
-    a.stages = a.quantized ? (per_cta < 3 ? per_cta : 3) : 0;
-    if (a.quantized && a.stages < 1) a.stages = 1;
+    // Grid: every CTA resident at once (a second wave would double the time).
+    // One CTA per tile when all tiles fit; otherwise a persistent grid with a
+    // ring of 2-4 stages, choosing the depth that keeps the most bytes in flight
+    // per SM (CTAs per SM x stages).
     const bool need_xf = IN != IN_QUANT || !a.quantized;
-    size_t smem = gemv_smem_bytes(a, need_xf);
-    while (a.quantized && smem > 200 * 1024 && a.stages > 1) {
-        a.stages--;
-        smem = gemv_smem_bytes(a, need_xf);
+    auto resident = [&](int stages, size_t *smem_out) {
+        a.stages = a.quantized ? stages : 0;
+        size_t smem = gemv_smem_bytes(a, need_xf, IN == IN_NORM);
+        *smem_out = smem;
+        int occ = 0;
+        if (smem > 200 * 1024 ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_kernel<IN, EPI>, GEMV_THREADS, smem) != cudaSuccess)
+            return 0;
+        return occ;
+    };
+    size_t smem = 0;
+    int grid = 0, best_stages = 1;
+    const int occ1 = resident(1, &smem);
+    if (occ1 <= 0) return set_err("gemv tile of %d x %d does not fit shared memory", R, a.cols);
+    if (total <= occ1 * n_sm || !a.quantized) {
+        grid = total < occ1 * n_sm ? total : occ1 * n_sm;
+    } else {
+        int best = 0;
+        for (int s = 2; s <= GEMV_MAX_STAGES; s++) {
+            size_t sm = 0;
+            const int occ = resident(s, &sm);
+            if (occ * s > best) { best = occ * s; best_stages = s; grid = occ * n_sm; }
+        }
+        if (best == 0) { best_stages = 1; grid = occ1 * n_sm; }
+        if (grid > total) grid = total;
     }
-    if (smem > 220 * 1024) return set_err("gemv tile of %d x %d does not fit shared memory", R, a.cols);
+    if (grid < 1) grid = 1;
+    resident(total <= grid ? 1 : best_stages, &smem);
     if (count) (*count)++;
     CK(launch_pdl(gemv_kernel<IN, EPI>, grid, GEMV_THREADS, smem, st, a));
     return 0;
@@ -871,3 +902,18 @@ extern "C" void ember_matmul_batch(float *out, const float *x, const void *w, in
     if (B <= 0) return;
     if (op_matmul(out, x, w, dtype, n_in, d_out, B, xq)) ember_die("cuda: %s", g_err);
 }
+
+#ifdef EMBER_PROBES
+// profiling build only: phase probes and per-launch wait times
+extern "C" int ember_cuda_probe_read(unsigned long long *phases, unsigned long long *waits, unsigned *count, int reset) {
+    if (cudaDeviceSynchronize() != cudaSuccess) return 1;
+    if (cudaMemcpyFromSymbol(phases, g_probe, sizeof(g_probe)) != cudaSuccess) return 1;
+    if (cudaMemcpyFromSymbol(count, g_wait_count, sizeof(unsigned)) != cudaSuccess) return 1;
+    if (cudaMemcpyFromSymbol(waits, g_wait_times, sizeof(g_wait_times)) != cudaSuccess) return 1;
+    if (reset) {
+        unsigned z = 0;
+        if (cudaMemcpyToSymbol(g_wait_count, &z, sizeof(z)) != cudaSuccess) return 1;
+    }
+    return 0;
+}
+#endif

@@ -3,14 +3,15 @@
  * The reference computes expf with the host C library (softmax, ref
  * src/model.c:61; SiLU, ref src/model.c:405), and its logits depend on every bit
  * of it. This file does not reproduce any library's expf. It evaluates exp(x) in
- * double precision with a textbook recipe:
+ * double precision with a textbook table-driven recipe:
  *
- *   k = nearest integer to x/ln2 (by the 1.5*2^52 shifter trick),
- *   r = (x - k*ln2_hi) - k*ln2_lo            (Cody & Waite range reduction),
- *   exp(r) by Horner on the degree-12 Taylor polynomial sum r^j/j!,
- *   exp(x) = exp(r) * 2^k,
+ *   k = nearest integer to x*64/ln2 (by the 1.5*2^52 shifter trick),
+ *   r = (x - k*hi) - k*lo, hi + lo = ln2/64   (Cody & Waite range reduction),
+ *   P(r) = sum_{j<=5} r^j/j! by Horner        (|r| <= ln2/128),
+ *   exp(x) = P(r) * 2^((k mod 64)/64) * 2^floor(k/64),
  *
- * and rounds the double to float. Its error is ~1e-8 float ulp, so it equals the
+ * with 2^(j/64) from a 64-entry table the host fills, and rounds the double to
+ * float. Its error is ~1e-8 float ulp, so it equals the
  * correctly rounded expf except very near a rounding midpoint. Where the C
  * library's result differs from it (it is within ~0.5 ulp but not always
  * correctly rounded), the input is listed in an exception table that the host
@@ -47,45 +48,37 @@ EXC_FN float exc_bitsf(uint32_t u) { union { float f; uint32_t u; } c; c.u = u; 
 /* exp(x) in double by the recipe above; x finite and within [p->lo, p->hi] */
 EXC_FN double exc_exp_double(const EmberExpfParams *p, float xf) {
     double x = (double)xf;
-    double t = EXC_ADD(EXC_MUL(x, p->inv_ln2), p->shifter);
-    double k = EXC_ADD(t, -p->shifter);
-    double r = EXC_ADD(EXC_ADD(x, -EXC_MUL(k, p->ln2_hi)), -EXC_MUL(k, p->ln2_lo));
-    double q = p->coef[12];
-    for (int j = 11; j >= 0; j--) q = EXC_ADD(EXC_MUL(q, r), p->coef[j]);
+    double t = EXC_ADD(EXC_MUL(x, p->inv_step), p->shifter);
+    double kd = EXC_ADD(t, -p->shifter);
+    int k = (int)kd;
+    double r = EXC_ADD(EXC_ADD(x, -EXC_MUL(kd, p->step_hi)), -EXC_MUL(kd, p->step_lo));
+    double q = p->coef[5];
+    for (int j = 4; j >= 0; j--) q = EXC_ADD(EXC_MUL(q, r), p->coef[j]);
+    int j = k & 63, m = (k - j) / 64;
     union { unsigned long long u; double d; } s;
-    s.u = (unsigned long long)((long long)k + 1023) << 52;
-    return EXC_MUL(q, s.d);
+    s.u = (unsigned long long)((long long)m + 1023) << 52;
+    return EXC_MUL(EXC_MUL(q, p->tab[j]), s.d);
+}
+
+EXC_FN unsigned long long exc_dbits(double d) { union { double d; unsigned long long u; } c; c.d = d; return c.u; }
+
+/* distance of a double y (whose float rounding r is normal, not FLT_MIN or
+ * FLT_MAX) from the nearest float rounding midpoint, in units of 2^-29 float ulp:
+ * the low 29 bits of y's mantissa are its position inside one float ulp */
+EXC_FN unsigned exc_mid_distance(double y) {
+    long long low = (long long)(exc_dbits(y) & ((1ull << 29) - 1)) - (1ll << 28);
+    return (unsigned)(low < 0 ? -low : low);
 }
 
 /* Round y (> 0) to float. *flag is set when the result may need the exception
- * table: y within p->delta ulps of a rounding midpoint, or a result that is not
- * a normal float below FLT_MAX. */
+ * table: y within the window of a rounding midpoint, or a result that is not a
+ * normal float strictly between FLT_MIN and FLT_MAX. */
 EXC_FN float exc_round(const EmberExpfParams *p, double y, int *flag) {
     float r = EXC_D2F(y);
     uint32_t rb = exc_fbits(r);
-    if (rb >= 0x7F7FFFFFu || rb < 0x00800000u) { *flag = 1; return r; }
-    double rd = (double)r;
-    uint32_t nb = (y >= rd) ? rb + 1u : rb - 1u;
-    double nd = (double)exc_bitsf(nb);
-    double mid = EXC_MUL(EXC_ADD(rd, nd), 0.5);
-    double ulp = nd > rd ? EXC_ADD(nd, -rd) : EXC_ADD(rd, -nd);
-    double dist = EXC_ADD(y, -mid);
-    if (dist < 0) dist = -dist;
-    *flag = dist < EXC_MUL(p->delta, ulp);
+    if (rb >= 0x7F7FFFFFu || rb <= 0x00800000u) { *flag = 1; return r; }
+    *flag = exc_mid_distance(y) < p->window;
     return r;
-}
-
-/* distance of y from the nearest midpoint in ulps (host table builder only) */
-EXC_FN double exc_midpoint_ulps(double y, float r) {
-    uint32_t rb = exc_fbits(r);
-    double rd = (double)r;
-    uint32_t nb = (y >= rd) ? rb + 1u : rb - 1u;
-    double nd = (double)exc_bitsf(nb);
-    double mid = EXC_MUL(EXC_ADD(rd, nd), 0.5);
-    double ulp = nd > rd ? EXC_ADD(nd, -rd) : EXC_ADD(rd, -nd);
-    double dist = EXC_ADD(y, -mid);
-    if (dist < 0) dist = -dist;
-    return dist / ulp;
 }
 
 EXC_FN uint32_t exc_hash(uint32_t xb, uint32_t n_slots) {

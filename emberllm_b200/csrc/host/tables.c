@@ -51,9 +51,9 @@ void ember_host_rope_table(float *out, int ctx, int head_dim, float theta) {
 #define SCAN_LO (-105.0f)
 #define SCAN_HI (90.0f)
 #define CACHE_MAGIC 0x46505845u /* "EXPF" */
-#define CACHE_VERSION 1u
+#define CACHE_VERSION 2u
 
-typedef struct { uint32_t x, y; double mid_ulps; int special; } Exc;
+typedef struct { uint32_t x, y; unsigned dist; int special; } Exc;
 
 typedef struct {
     const EmberExpfParams *p;
@@ -67,21 +67,25 @@ static pthread_mutex_t g_lock = PTHREAD_MUTEX_INITIALIZER;
 static int g_ready = 0;
 static EmberExpfParams g_params;
 static uint32_t *g_slots = NULL;
+static double g_tab[64];
 
 static void fill_constants(EmberExpfParams *p) {
     memset(p, 0, sizeof(*p));
     double c = 1.0;
     p->coef[0] = 1.0;
-    for (int j = 1; j <= 12; j++) { c = c / (double)j; p->coef[j] = c; }
+    for (int j = 1; j <= 5; j++) { c = c / (double)j; p->coef[j] = c; }
+    const double step = M_LN2 / 64.0;            /* exact: a power-of-two division */
     union { double d; uint64_t u; } hi;
-    hi.d = M_LN2;
-    hi.u &= ~((1ull << 28) - 1);                 /* 25 significant bits: k*ln2_hi is exact */
-    p->ln2_hi = hi.d;
-    p->ln2_lo = M_LN2 - hi.d;                    /* exact (Sterbenz) */
-    p->inv_ln2 = 1.0 / M_LN2;
+    hi.d = step;
+    hi.u &= ~((1ull << 20) - 1);                 /* 33 significant bits: k*step_hi is exact */
+    p->step_hi = hi.d;
+    p->step_lo = step - hi.d;                    /* exact (Sterbenz) */
+    p->inv_step = 64.0 / M_LN2;
     p->shifter = 6755399441055744.0;             /* 1.5 * 2^52 */
     p->lo = SCAN_LO;
     p->hi = SCAN_HI;
+    for (int j = 0; j < 64; j++) g_tab[j] = exp2((double)j / 64.0);
+    p->tab = g_tab;
 }
 
 /* scan space: [0, npos) are +0 .. SCAN_HI, then -0 .. SCAN_LO */
@@ -114,8 +118,8 @@ static void *scan_worker(void *arg) {
         Exc *e = &j->list[j->n++];
         e->x = xb;
         e->y = gb;
-        e->special = (rb >= 0x7F7FFFFFu || rb < 0x00800000u);
-        e->mid_ulps = e->special ? 0.0 : exc_midpoint_ulps(y, r);
+        e->special = (rb >= 0x7F7FFFFFu || rb <= 0x00800000u);
+        e->dist = e->special ? 0u : exc_mid_distance(y);
     }
     return NULL;
 }
@@ -145,8 +149,9 @@ static uint64_t fingerprint(void) {
     EmberExpfParams p;
     fill_constants(&p);
     h = fnv(h, p.coef, sizeof(p.coef));
-    h = fnv(h, &p.ln2_hi, sizeof(double));
-    h = fnv(h, &p.ln2_lo, sizeof(double));
+    h = fnv(h, &p.step_hi, sizeof(double));
+    h = fnv(h, &p.step_lo, sizeof(double));
+    h = fnv(h, g_tab, sizeof(g_tab));
     return h;
 }
 
@@ -190,16 +195,15 @@ static int load_cache(const char *path, uint64_t fp, EmberExpfParams *p, uint32_
                       uint32_t *n) {
     FILE *f = fopen(path, "rb");
     if (!f) return 1;
-    uint32_t magic = 0, ver = 0, cnt = 0;
+    uint32_t magic = 0, ver = 0, cnt = 0, window = 0;
     uint64_t cfp = 0;
-    double delta = 0;
     int rc = 1;
     if (fread(&magic, 4, 1, f) == 1 && fread(&ver, 4, 1, f) == 1 && fread(&cfp, 8, 1, f) == 1 &&
-        fread(&cnt, 4, 1, f) == 1 && fread(&delta, 8, 1, f) == 1 && magic == CACHE_MAGIC &&
+        fread(&cnt, 4, 1, f) == 1 && fread(&window, 4, 1, f) == 1 && magic == CACHE_MAGIC &&
         ver == CACHE_VERSION && cfp == fp && cnt < (1u << 26)) {
         uint32_t *buf = malloc((size_t)cnt * 8 + 8);
         if (buf && fread(buf, 8, cnt, f) == cnt) {
-            p->delta = delta;
+            p->window = window;
             if (verify(p, buf, cnt) == 0) { *pairs = buf; *n = cnt; rc = 0; }
         }
         if (rc) free(buf);
@@ -208,7 +212,7 @@ static int load_cache(const char *path, uint64_t fp, EmberExpfParams *p, uint32_
     return rc;
 }
 
-static void save_cache(const char *path, uint64_t fp, double delta, const uint32_t *pairs,
+static void save_cache(const char *path, uint64_t fp, uint32_t window, const uint32_t *pairs,
                        uint32_t n) {
     mkdirs(path);
     char tmp[1100];
@@ -218,7 +222,7 @@ static void save_cache(const char *path, uint64_t fp, double delta, const uint32
     uint32_t magic = CACHE_MAGIC, ver = CACHE_VERSION;
     int ok = fwrite(&magic, 4, 1, f) == 1 && fwrite(&ver, 4, 1, f) == 1 &&
              fwrite(&fp, 8, 1, f) == 1 && fwrite(&n, 4, 1, f) == 1 &&
-             fwrite(&delta, 8, 1, f) == 1 && fwrite(pairs, 8, n, f) == n;
+             fwrite(&window, 4, 1, f) == 1 && fwrite(pairs, 8, n, f) == n;
     if (fclose(f) != 0) ok = 0;
     if (ok) rename(tmp, path);
     else unlink(tmp);
@@ -250,13 +254,13 @@ static int scan(EmberExpfParams *p, uint32_t **pairs_out, uint32_t *n_out) {
     free(started);
     size_t n = 0;
     int bad = 0;
-    double worst = 0;
+    unsigned worst = 0;
     for (int t = 0; t < nt; t++) {
         bad |= jobs[t].oom;
         n += jobs[t].n;
         for (size_t i = 0; i < jobs[t].n; i++)
-            if (!jobs[t].list[i].special && jobs[t].list[i].mid_ulps > worst)
-                worst = jobs[t].list[i].mid_ulps;
+            if (!jobs[t].list[i].special && jobs[t].list[i].dist > worst)
+                worst = jobs[t].list[i].dist;
     }
     uint32_t *pairs = bad ? NULL : malloc(n * 8 + 8);
     if (pairs) {
@@ -272,8 +276,8 @@ static int scan(EmberExpfParams *p, uint32_t **pairs_out, uint32_t *n_out) {
     free(jobs);
     free(th);
     if (!pairs) return 1;
-    p->delta = worst * 2.0 > 1e-6 ? worst * 2.0 : 1e-6;
-    while (verify(p, pairs, (uint32_t)n) != 0 && p->delta < 0.5) p->delta *= 2.0;
+    /* a listed input is flagged when its distance is below the window */
+    p->window = worst * 2u + 64u;
     if (verify(p, pairs, (uint32_t)n) != 0) { free(pairs); return 1; }
     *pairs_out = pairs;
     *n_out = (uint32_t)n;
@@ -300,7 +304,7 @@ int ember_host_expf_params(EmberExpfParams *out) {
         int nocache = getenv("EMBER_EXPF_NOCACHE") && atoi(getenv("EMBER_EXPF_NOCACHE")) != 0;
         if (nocache || load_cache(path, fp, &p, &pairs, &n) != 0) {
             if (scan(&p, &pairs, &n) != 0) { pthread_mutex_unlock(&g_lock); return 1; }
-            if (!nocache) save_cache(path, fp, p.delta, pairs, n);
+            if (!nocache) save_cache(path, fp, p.window, pairs, n);
         }
         uint32_t slots = 1024;
         while (slots < 2u * n + 2u) slots <<= 1;

@@ -48,21 +48,26 @@ typedef struct {
 } EmberCudaModelDesc;
 
 /* Parameters of the device expf. The device computes exp(x) with a fixed
- * double-precision recipe (range reduction by ln2 in two parts + a degree-12
- * Taylor polynomial, all constants supplied by the host so host and device use
- * identical bits) and rounds to float. The host scans every float input in
- * [lo, hi] once against the C library's expf and lists, in an open-addressing
- * table, the inputs where the library's result differs; the device consults the
- * table only when its double result lies within `delta` float-ulps of a rounding
- * midpoint (every listed input satisfies this by construction) or the result is
+ * double-precision recipe -- k = nearest integer to x*64/ln2, r = x - k*ln2/64
+ * (ln2/64 in two parts), exp(x) = 2^(k>>6) * 2^((k&63)/64) * P(r) with P the
+ * degree-5 Taylor polynomial and 2^(j/64) from a 64-entry table -- and rounds to
+ * float. All constants and the table come from the host, so host and device
+ * compute identical bits. The host scans every float input in [lo, hi] once
+ * against the C library's expf and lists, in an open-addressing table, the
+ * inputs where the library's result differs; the device consults the table only
+ * when the double result lies within `window` units of 2^-29 float ulp of a
+ * rounding midpoint (every listed input does, by construction) or the result is
  * not a normal float. Below lo the result is +0, above hi it is +inf. */
 typedef struct {
-    double coef[13];        /* polynomial coefficients, coef[k] ~ 1/k!                */
-    double inv_ln2, ln2_hi, ln2_lo, shifter;
-    double delta;           /* midpoint window, in float ulps                         */
+    double coef[6];         /* polynomial coefficients, coef[k] ~ 1/k!                */
+    double inv_step;        /* 64 / ln2                                               */
+    double step_hi, step_lo;/* ln2 / 64 split so that k * step_hi is exact            */
+    double shifter;         /* 1.5 * 2^52: rounds to the nearest integer              */
+    uint32_t window;        /* midpoint window, units of 2^-29 float ulp              */
     float  lo, hi;          /* scanned input range                                    */
     uint32_t n_slots;       /* power of two                                           */
     uint32_t n_entries;
+    const double *tab;      /* 64 doubles, 2^(j/64)                                   */
     const uint32_t *slots;  /* 2*n_slots words: (x bits, expf bits); empty key = ~0u */
 } EmberExpfParams;
 

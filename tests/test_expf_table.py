@@ -13,11 +13,13 @@ from . import helpers as H
 
 
 class Params(ctypes.Structure):
-    _fields_ = [("coef", ctypes.c_double * 13), ("inv_ln2", ctypes.c_double),
-                ("ln2_hi", ctypes.c_double), ("ln2_lo", ctypes.c_double),
-                ("shifter", ctypes.c_double), ("delta", ctypes.c_double),
+    """EmberExpfParams (include/ember_cuda.h)"""
+    _fields_ = [("coef", ctypes.c_double * 6), ("inv_step", ctypes.c_double),
+                ("step_hi", ctypes.c_double), ("step_lo", ctypes.c_double),
+                ("shifter", ctypes.c_double), ("window", ctypes.c_uint32),
                 ("lo", ctypes.c_float), ("hi", ctypes.c_float),
                 ("n_slots", ctypes.c_uint32), ("n_entries", ctypes.c_uint32),
+                ("tab", ctypes.POINTER(ctypes.c_double)),
                 ("slots", ctypes.POINTER(ctypes.c_uint32))]
 
 
@@ -54,7 +56,7 @@ def test_table_is_nontrivial(params):
     _, p = params
     assert p.n_entries > 1000               # the library's expf is not correctly rounded
     assert p.n_slots >= 2 * p.n_entries     # at most half full
-    assert 0 < p.delta < 0.05
+    assert 0 < p.window < (1 << 29) // 100  # a small fraction of an ulp
 
 
 def test_listed_inputs_and_neighbours(params):
