@@ -53,6 +53,14 @@ def parse():
     p.add_argument("--tokens", type=int, default=128)
     p.add_argument("--e2e-steps", type=int, default=2)
     p.add_argument("--cpu-baseline", type=int, default=1)
+    p.add_argument("--nvtx", action="store_true",
+                   help="mark the timed region (and --kernel-case launches) as NVTX ranges "
+                        "'timed' / 'case' for ncu --nvtx-include")
+    p.add_argument("--kernel-case", type=int, default=-1,
+                   help="profiling case: one decode position at --depth, then one untimed and "
+                        "one timed round of kernel kind K (%s) over every layer; prints "
+                        "its time and bytes and exits" % ", ".join(
+                            "%d %s" % kv for kv in enumerate(KIND_NAMES)))
     return p.parse_args()
 
 
@@ -68,14 +76,16 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
-def ncu_traffic(kind_name, config):
-    """per-launch DRAM bytes from the committed ncu summary (profiles/), or None"""
+def ncu_traffic(kind_name, config, pos):
+    """per-launch DRAM bytes (read + write) of one kernel kind at one decode
+    position, from the committed ncu summary profiles/dram_traffic.txt, or None"""
     path = os.path.join(ROOT, "profiles", "dram_traffic.txt")
     try:
         for line in open(path):
             parts = line.split()
-            if len(parts) >= 3 and parts[0] == kind_name and parts[1] == config:
-                return float(parts[2])
+            if len(parts) >= 4 and parts[0] == kind_name and parts[1] == config \
+                    and parts[2] == str(pos):
+                return float(parts[3])
     except OSError:
         pass
     return None
@@ -203,6 +213,24 @@ def dist_setup(args):
     return 1, 0, 0, None
 
 
+class Nvtx:
+    """NVTX push/pop ranges (through torch's bindings) when --nvtx is given"""
+
+    def __init__(self, on):
+        self.nvtx = None
+        if on:
+            import torch.cuda.nvtx as nvtx
+            self.nvtx = nvtx
+
+    def push(self, name):
+        if self.nvtx:
+            self.nvtx.range_push(name)
+
+    def pop(self):
+        if self.nvtx:
+            self.nvtx.range_pop()
+
+
 def barrier(dist):
     if dist is not None:
         dist.barrier()
@@ -242,6 +270,21 @@ def run_ours(args, world, rank, local, dist):
     depth, ntok = args.depth, args.tokens
     e = Ember(path, ctx=depth + ntok + 8)
     cs = lib.ember_state_cuda(e.st)
+    nvtx = Nvtx(args.nvtx)
+    # kernels are timed alone at the step's mean position (attention length)
+    kpos = depth + ntok // 2
+    if args.kernel_case >= 0:
+        # one decode position at kpos (sets the attended length), then the kernel kind
+        e.forward(0, kpos)
+        ms, by = ctypes.c_float(), ctypes.c_double()
+        nvtx.push("case")
+        rc = lib.ember_cuda_time_kernel(cs, args.kernel_case, 1, ctypes.byref(ms), ctypes.byref(by))
+        nvtx.pop()
+        assert rc == 0, lib.ember_cuda_error()
+        e.close()
+        return {"kernel_case": KIND_NAMES[args.kernel_case], "config": args.config, "pos": kpos,
+                "us_per_launch": round(ms.value * 1e3, 3), "bytes_per_launch": int(by.value),
+                "launches": 2 * (1 if args.kernel_case == 5 else cfg["n_layers"])}
     rng = np.random.default_rng(1)
     prompt = [int(t) for t in rng.integers(0, e.vocab, depth)]
 
@@ -263,10 +306,12 @@ def run_ours(args, world, rank, local, dist):
     clocks = ClockSampler(local)
     clocks.start()
     barrier(dist)
+    nvtx.push("timed")
     lib.ember_cuda_mark(cs, 0)
     for _ in range(args.steps):
         e.greedy(first, depth, ntok)
     lib.ember_cuda_mark(cs, 1)
+    nvtx.pop()
     t = elapsed(0, 1)
     clk = clocks.stop()
     t_max = max_over_ranks(dist, t)
@@ -282,7 +327,8 @@ def run_ours(args, world, rank, local, dist):
     lib.ember_cuda_mark(cs, 3)
     t_e2e = max_over_ranks(dist, elapsed(2, 3))
 
-    # roofline of the dominant kernel kind, timed live (overwrites the state)
+    # roofline of the dominant kernel kind, timed live at kpos (overwrites the state)
+    e.forward(0, kpos)
     kinds = []
     L = cfg["n_layers"]
     for kind in range(6):
@@ -334,7 +380,7 @@ def run_ours(args, world, rank, local, dist):
         "roofline": {"kernel": KIND_NAMES[dk], "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
                      "frac": round(achieved / peak, 4),
-                     "traffic": ncu_traffic(KIND_NAMES[dk], args.config),
+                     "traffic": ncu_traffic(KIND_NAMES[dk], args.config, kpos), "pos": kpos,
                      "bytes_per_launch": int(dbytes), "us_per_launch": round(dms * 1e3, 3)},
         "kernel_shares": {KIND_NAMES[k]: round(ps, 4) for ps, k, _, _ in kinds},
         "clocks": clk,
