@@ -236,8 +236,20 @@ EMB_DEV void prefetch_l2(const void *p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// KV cache element access: the cache holds fp32 as is, or fp16 rounded to
+// nearest even (ref src/model.c:43, ember_f16c); reads widen to fp32
+EMB_DEV float widen(float v) { return v; }
+EMB_DEV float widen(__half v) { return __half2float(v); }
+EMB_DEV void kv_round(float v, float *out) { *out = v; }
+EMB_DEV void kv_round(float v, __half *out) { *out = __float2half_rn(v); }
+
+// ctl words in device memory, read by the step's kernels (so one captured graph
+// serves every position): pos, token, number of greedy tokens written, position
+// of ids[0] during a prefill, and the device error word.
+enum { CTL_POS = 0, CTL_TOK = 1, CTL_NOUT = 2, CTL_BASE = 3, CTL_ERR = 4, CTL_WORDS = 8 };
+
 // device error codes (written to the state's error word, read by the host)
-enum { ERR_NONE = 0, ERR_GEMV_WAIT = 1, ERR_ATTN_WAIT = 2 };
+enum { ERR_NONE = 0, ERR_GEMV_WAIT = 1, ERR_ATTN_WAIT = 2, ERR_PF_WAIT = 3 };
 
 // The device expf: the host C library's expf, reproduced from the recipe and
 // exception table described in expf_core.h.

@@ -38,10 +38,6 @@ constexpr int ATTN_THREADS = 256;
 enum { IN_RAW = 0, IN_NORM = 1, IN_QUANT = 2 };
 enum { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2 };
 
-// ctl words in device memory, read by the step's kernels (so one captured graph
-// serves every position): pos, token, number of greedy tokens written, position
-// of ids[0] during a prefill, and the device error word.
-enum { CTL_POS = 0, CTL_TOK = 1, CTL_NOUT = 2, CTL_BASE = 3, CTL_ERR = 4, CTL_WORDS = 8 };
 
 // A weight matrix in the device layout: rows of quantized bytes (Q8_0: 32 int8
 // per block; Q4_0: 16 bytes per block, nibble order as in the file) and, apart,
@@ -410,12 +406,6 @@ struct AttnArgs {
     ExpfDev ex;
 };
 
-EMB_DEV float widen(float v) { return v; }
-EMB_DEV float widen(__half v) { return __half2float(v); }
-// the value stored in the cache: fp32 as is, or fp16 rounded to nearest even
-// (ref src/model.c:43, ember_f16c)
-EMB_DEV void kv_round(float v, float *out) { *out = v; }
-EMB_DEV void kv_round(float v, __half *out) { *out = __float2half_rn(v); }
 
 // Copy keys of positions [c0, c0+n) (all hd rows of the transposed layout) into
 // kbuf[hd][CH] with 16-byte loads by all threads, eight in flight per thread.

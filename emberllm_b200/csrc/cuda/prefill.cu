@@ -1,0 +1,468 @@
+// prefill.cu — host side of the batched prefill (ref src/model.c:283-360) and of
+// the op-level ember_matmul_batch (ref src/kernels.c:227-264).
+//
+// Weight packs. The first batched prefill on a model builds, per layer, four
+// int8 matrices in the layout the tensor-core GEMM reads through TMA: q|k|v rows
+// concatenated (one GEMM), wo, w1|w3 concatenated (one GEMM, SwiGLU reads both
+// halves of a row), w2. Rows are padded to a multiple of 128 and K to a multiple
+// of 128 bytes (zeros), Q4_0 nibbles are expanded to int8 (q - 8), and the
+// block scales are widened to fp32 rows [rows_pad][nbp]. The packs are a second
+// copy of the layer weights (the decode path keeps the compact Q8_0 / Q4_0 rows).
+//
+// Activations. A state's prefill scratch holds PF_CHUNK tokens: the residual
+// stream X [n][dim], the int8 GEMM input XQ [n_pad][k_pad] with its block scales
+// XS [nb][n_pad], the q|k|v output, the roped queries and the w1|w3 output.
+// Longer prompts run in chunks of PF_CHUNK tokens (the per-token arithmetic does
+// not depend on how tokens are grouped).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+#include <vector>
+
+#include "ember_ops.h"
+#include "prefill_kernels.cuh"
+#include "runtime_internal.cuh"
+
+namespace emb {
+
+constexpr int PF_CHUNK = 512;              // tokens per batched pass
+constexpr int PF_BNS[3] = { 32, 64, 128 };
+
+static size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
+
+// ------------------------------------------------------------ tensor maps ----
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    });
+    return fn;
+}
+
+// an int8 matrix [outer][inner] (row stride = inner bytes) read in boxes of
+// 128 bytes x box_rows rows with 128-byte swizzle
+static int map_i8(CUtensorMap *map, const void *base, size_t inner, size_t outer, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return set_err("cuTensorMapEncodeTiled is not available from the driver");
+    if (inner % 128 || (uintptr_t)base % 16) return set_err("tensor map: unaligned int8 matrix");
+    cuuint64_t dims[2] = { (cuuint64_t)inner, (cuuint64_t)outer };
+    cuuint64_t strides[1] = { (cuuint64_t)inner };
+    cuuint32_t box[2] = { 128u, (cuuint32_t)box_rows };
+    cuuint32_t es[2] = { 1u, 1u };
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_err("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return 0;
+}
+
+// ------------------------------------------------------------ kernel setup ---
+
+template <typename K>
+static int pf_allow_smem(K kernel, int bytes) {
+    CK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    return 0;
+}
+
+static int g_att_smem_cap = 0;   // dynamic smem the attention kernel may use
+
+static int pf_init(int device) {
+    static unsigned done = 0;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    if (device < 32 && ((done >> device) & 1u)) return 0;
+    int optin = 0;
+    CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+    if (pf_allow_smem(pf_gemm_kernel<32, PF_EPI_STORE>, PfLayout<32>::SMEM) ||
+        pf_allow_smem(pf_gemm_kernel<32, PF_EPI_RESID>, PfLayout<32>::SMEM) ||
+        pf_allow_smem(pf_gemm_kernel<64, PF_EPI_STORE>, PfLayout<64>::SMEM) ||
+        pf_allow_smem(pf_gemm_kernel<64, PF_EPI_RESID>, PfLayout<64>::SMEM) ||
+        pf_allow_smem(pf_gemm_kernel<128, PF_EPI_STORE>, PfLayout<128>::SMEM) ||
+        pf_allow_smem(pf_gemm_kernel<128, PF_EPI_RESID>, PfLayout<128>::SMEM))
+        return 1;
+    cudaFuncAttributes fa;
+    CK(cudaFuncGetAttributes(&fa, pf_attn_kernel<float>));
+    int cap = optin - (int)fa.sharedSizeBytes;
+    CK(cudaFuncGetAttributes(&fa, pf_attn_kernel<__half>));
+    if (optin - (int)fa.sharedSizeBytes < cap) cap = optin - (int)fa.sharedSizeBytes;
+    if (pf_allow_smem(pf_attn_kernel<float>, cap) || pf_allow_smem(pf_attn_kernel<__half>, cap)) return 1;
+    g_att_smem_cap = cap;
+    if (device < 32) done |= 1u << device;
+    return 0;
+}
+
+// ------------------------------------------------------------ weight packs ---
+
+struct PfMat {
+    int8_t *q = nullptr;
+    float *s = nullptr;
+    int rows = 0, rows_pad = 0, k = 0, k_pad = 0, nb = 0, nbp = 0;
+    CUtensorMap map;           // A operand: boxes of 128 rows x 128 bytes
+};
+
+struct PfLayerPack {
+    PfMat qkv, wo, w13, w2;
+};
+
+struct PfModel {
+    std::vector<PfLayerPack> layers;
+    std::vector<void *> allocs;
+};
+
+static int pf_alloc(std::vector<void *> &v, void **p, size_t n) {
+    CK(cudaMalloc(p, n ? n : 16));
+    v.push_back(*p);
+    return 0;
+}
+
+// concatenate the row blocks of `parts` (same cols, quantized) into one pack
+static int build_pack(PfModel *pm, PfMat *pk, const DevMat *const *parts, int nparts) {
+    const int k = parts[0]->cols;
+    int rows = 0;
+    for (int i = 0; i < nparts; i++) {
+        if (parts[i]->cols != k || parts[i]->dtype == EMBER_DT_F32) return set_err("prefill pack: bad matrix");
+        rows += parts[i]->rows;
+    }
+    pk->rows = rows;
+    pk->rows_pad = (int)round_up((size_t)rows, PF_BM);
+    pk->k = k;
+    pk->k_pad = (int)round_up((size_t)k, PF_BK);
+    pk->nb = k / 32;
+    pk->nbp = (int)round_up((size_t)pk->nb, 4);
+    const size_t qbytes = (size_t)pk->rows_pad * pk->k_pad, sbytes = (size_t)pk->rows_pad * pk->nbp * 4;
+    if (pf_alloc(pm->allocs, (void **)&pk->q, qbytes) || pf_alloc(pm->allocs, (void **)&pk->s, sbytes)) return 1;
+    CK(cudaMemset(pk->q, 0, qbytes));
+    CK(cudaMemset(pk->s, 0, sbytes));
+    int r0 = 0;
+    for (int i = 0; i < nparts; i++) {
+        PfPackArgs a;
+        a.q = parts[i]->q; a.s = parts[i]->s; a.dtype = parts[i]->dtype; a.rows = parts[i]->rows; a.nb = pk->nb;
+        a.dq = pk->q + (size_t)r0 * pk->k_pad; a.ds = pk->s + (size_t)r0 * pk->nbp;
+        a.k_pad = pk->k_pad; a.nbp = pk->nbp;
+        const long long total = (long long)a.rows * a.nb;
+        const int grid = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+        pf_pack_kernel<<<grid > 0 ? grid : 1, 256>>>(a);
+        CK(cudaGetLastError());
+        r0 += parts[i]->rows;
+    }
+    return map_i8(&pk->map, pk->q, (size_t)pk->k_pad, (size_t)pk->rows_pad, PF_BM);
+}
+
+int pf_supported(const EmberCudaModel *m) {
+    if (m->head_dim > 256 || m->head_dim % 32) return 0;
+    if (m->n_heads / m->n_kv > PF_ATT_MAX_ROWS) return 0;
+    for (const DevLayer &L : m->layers) {
+        const DevMat *mats[7] = { &L.wq, &L.wk, &L.wv, &L.wo, &L.w1, &L.w2, &L.w3 };
+        for (const DevMat *d : mats)
+            if (d->dtype != EMBER_DT_Q8_0 && d->dtype != EMBER_DT_Q4_0) return 0;
+    }
+    return 1;
+}
+
+static int pf_prepare_model(EmberCudaModel *m) {
+    if (m->pf) return 0;
+    if (pf_init(m->device)) return 1;
+    PfModel *pm = new PfModel();
+    pm->layers.resize(m->layers.size());
+    int rc = 0;
+    for (size_t l = 0; l < m->layers.size() && !rc; l++) {
+        const DevLayer &L = m->layers[l];
+        PfLayerPack &P = pm->layers[l];
+        const DevMat *qkv[3] = { &L.wq, &L.wk, &L.wv };
+        const DevMat *wo[1] = { &L.wo };
+        const DevMat *w13[2] = { &L.w1, &L.w3 };
+        const DevMat *w2[1] = { &L.w2 };
+        rc = build_pack(pm, &P.qkv, qkv, 3) || build_pack(pm, &P.wo, wo, 1) || build_pack(pm, &P.w13, w13, 2) ||
+             build_pack(pm, &P.w2, w2, 1);
+    }
+    if (!rc && cudaDeviceSynchronize() != cudaSuccess) rc = set_err("prefill pack build failed");
+    if (rc) {
+        for (void *p : pm->allocs) cudaFree(p);
+        delete pm;
+        return 1;
+    }
+    m->pf = pm;
+    return 0;
+}
+
+void pf_model_release(EmberCudaModel *m) {
+    if (!m || !m->pf) return;
+    for (void *p : m->pf->allocs) cudaFree(p);
+    delete m->pf;
+    m->pf = nullptr;
+}
+
+// ------------------------------------------------------------ state scratch --
+
+enum { PF_K_DIM = 0, PF_K_QD = 1, PF_K_HID = 2 };
+
+struct PfState {
+    int n_cap = 0, n_pad = 0;
+    int k_pad[3] = { 0, 0, 0 };
+    float *X = nullptr, *XS = nullptr, *QKV = nullptr, *QR = nullptr, *H = nullptr;
+    int8_t *XQ = nullptr;
+    int ld_qkv = 0, ld_h = 0;
+    CUtensorMap mapB[3][3];    // [K kind][BN index]
+    std::vector<void *> allocs;
+};
+
+static int pf_prepare_state(EmberCudaState *s) {
+    if (s->pf) return 0;
+    EmberCudaModel *m = s->m;
+    PfState *ps = new PfState();
+    const int hd = m->head_dim, qd = m->n_heads * hd, kvd = m->n_kv * hd;
+    ps->n_cap = PF_CHUNK;
+    ps->n_pad = (int)round_up(PF_CHUNK, 128);
+    const int ks[3] = { m->dim, qd, m->hidden };
+    size_t kmax = 0;
+    int nbmax = 0;
+    for (int i = 0; i < 3; i++) {
+        ps->k_pad[i] = (int)round_up((size_t)ks[i], PF_BK);
+        if ((size_t)ps->k_pad[i] > kmax) kmax = ps->k_pad[i];
+        if (ks[i] / 32 > nbmax) nbmax = ks[i] / 32;
+    }
+    const PfLayerPack &P0 = m->pf->layers[0];
+    ps->ld_qkv = P0.qkv.rows_pad;
+    ps->ld_h = P0.w13.rows_pad;
+    (void)kvd;
+    int rc = pf_alloc(ps->allocs, (void **)&ps->X, (size_t)ps->n_cap * m->dim * 4) ||
+             pf_alloc(ps->allocs, (void **)&ps->XQ, (size_t)ps->n_pad * kmax) ||
+             pf_alloc(ps->allocs, (void **)&ps->XS, (size_t)nbmax * ps->n_pad * 4) ||
+             pf_alloc(ps->allocs, (void **)&ps->QKV, (size_t)ps->n_cap * ps->ld_qkv * 4) ||
+             pf_alloc(ps->allocs, (void **)&ps->QR, (size_t)ps->n_cap * qd * 4) ||
+             pf_alloc(ps->allocs, (void **)&ps->H, (size_t)ps->n_cap * ps->ld_h * 4);
+    if (!rc && (cudaMemset(ps->XQ, 0, (size_t)ps->n_pad * kmax) != cudaSuccess ||
+                cudaMemset(ps->XS, 0, (size_t)nbmax * ps->n_pad * 4) != cudaSuccess))
+        rc = set_err("prefill scratch initialisation failed");
+    for (int i = 0; i < 3 && !rc; i++)
+        for (int j = 0; j < 3 && !rc; j++)
+            rc = map_i8(&ps->mapB[i][j], ps->XQ, (size_t)ps->k_pad[i], (size_t)ps->n_pad, PF_BNS[j]);
+    if (rc) {
+        for (void *p : ps->allocs) cudaFree(p);
+        delete ps;
+        return 1;
+    }
+    s->pf = ps;
+    return 0;
+}
+
+void pf_state_release(EmberCudaState *s) {
+    if (!s || !s->pf) return;
+    for (void *p : s->pf->allocs) cudaFree(p);
+    delete s->pf;
+    s->pf = nullptr;
+}
+
+// ------------------------------------------------------------ launches -------
+
+// Token-tile width: the one that minimises the busiest SM's share of tile-
+// columns (the epilogue's fp32 work grows with the width), counting the CTAs
+// each SM holds at once.
+static int choose_bn(int rows_pad, int n, int n_sm) {
+    int best = 2;
+    long long best_cost = -1;
+    for (int j = 2; j >= 0; j--) {
+        const int bn = PF_BNS[j];
+        const int occ = bn == 128 ? 1 : 2;
+        const long long tiles = (long long)(rows_pad / PF_BM) * ((n + bn - 1) / bn);
+        const long long waves = (tiles + (long long)n_sm * occ - 1) / ((long long)n_sm * occ);
+        const long long cost = waves * occ * bn;
+        if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = j; }
+    }
+    return best;
+}
+
+template <int BN, int EPI>
+static int launch_gemm_bn(const PfMat &w, const CUtensorMap &mb, const PfGemmArgs &a, cudaStream_t st) {
+    dim3 grid((unsigned)(w.rows_pad / PF_BM), (unsigned)((a.n + BN - 1) / BN));
+    pf_gemm_kernel<BN, EPI><<<grid, PfLayout<BN>::THREADS, PfLayout<BN>::SMEM, st>>>(w.map, mb, a);
+    CK(cudaGetLastError());
+    return 0;
+}
+
+static int launch_gemm(const PfMat &w, const CUtensorMap (&maps)[3], const float *xs, int n_pad, int n,
+                       float *out, int ld, bool resid, int *err, int n_sm, cudaStream_t st) {
+    PfGemmArgs a;
+    a.ws = w.s; a.xs = xs; a.out = out; a.err = err;
+    a.rows = w.rows; a.nb = w.nb; a.nbp = w.nbp; a.n = n; a.n_pad = n_pad; a.ld = ld;
+    const int j = choose_bn(w.rows_pad, n, n_sm);
+    switch (j * 2 + (resid ? 1 : 0)) {
+    case 0: return launch_gemm_bn<32, PF_EPI_STORE>(w, maps[0], a, st);
+    case 1: return launch_gemm_bn<32, PF_EPI_RESID>(w, maps[0], a, st);
+    case 2: return launch_gemm_bn<64, PF_EPI_STORE>(w, maps[1], a, st);
+    case 3: return launch_gemm_bn<64, PF_EPI_RESID>(w, maps[1], a, st);
+    case 4: return launch_gemm_bn<128, PF_EPI_STORE>(w, maps[2], a, st);
+    default: return launch_gemm_bn<128, PF_EPI_RESID>(w, maps[2], a, st);
+    }
+}
+
+// attention tile: tokens per CTA so that rows * positions fit shared memory
+static int attn_tile(const EmberCudaModel *m, int p_cap, int *tq) {
+    const int kv_mul = m->n_heads / m->n_kv;
+    int t = PF_ATT_MAX_ROWS / kv_mul;
+    while (t > 0 && (size_t)t * kv_mul * p_cap * 4 > (size_t)g_att_smem_cap) t--;
+    *tq = t;
+    return t > 0;
+}
+
+int pf_run_layers(EmberCudaState *s, const int *ids_dev, int n, int start) {
+    EmberCudaModel *m = s->m;
+    if (pf_prepare_model(m) || pf_prepare_state(s)) return 1;
+    PfState *ps = s->pf;
+    cudaStream_t st = s->stream;
+    int *err = s->ctl + CTL_ERR;
+    const int hd = m->head_dim, qd = m->n_heads * hd;
+    const size_t es = s->kv_fp16 ? 2 : 4;
+    int tq = 0;
+    const int p_cap = (int)round_up((size_t)(start + n), 4);
+    if (!attn_tile(m, p_cap, &tq)) return set_err("prefill: %d positions do not fit the attention tile", start + n);
+    int nc = 0;
+    for (int c0 = 0; c0 < n; c0 += ps->n_cap) {
+        nc = n - c0 < ps->n_cap ? n - c0 : ps->n_cap;
+        const int st0 = start + c0;
+        {
+            PfEmbedArgs ea;
+            ea.q = m->tok_emb.q; ea.s = m->tok_emb.s; ea.dtype = m->tok_emb.dtype; ea.dim = m->dim;
+            ea.vocab = m->vocab; ea.ids = ids_dev + c0; ea.x = ps->X; ea.err = err;
+            pf_embed_kernel<<<nc, 256, 0, st>>>(ea);
+            CK(cudaGetLastError());
+        }
+        for (int l = 0; l < m->n_layers; l++) {
+            const DevLayer &L = m->layers[l];
+            const PfLayerPack &P = m->pf->layers[l];
+            PfTokArgs ta;
+            memset(&ta, 0, sizeof(ta));
+            ta.xq = ps->XQ; ta.xs = ps->XS; ta.n_pad = ps->n_pad; ta.ex = m->ex; ta.eps = m->eps;
+            // attention block
+            ta.x = ps->X; ta.ld_x = m->dim; ta.norm_w = L.attn_norm; ta.cols = m->dim; ta.k_pad = ps->k_pad[PF_K_DIM];
+            pf_norm_quant_kernel<<<nc, 256, (size_t)m->dim * 4, st>>>(ta);
+            CK(cudaGetLastError());
+            if (launch_gemm(P.qkv, ps->mapB[PF_K_DIM], ps->XS, ps->n_pad, nc, ps->QKV, ps->ld_qkv, false, err,
+                            m->n_sm, st))
+                return 1;
+            PfQkvArgs qa;
+            qa.qkv = ps->QKV; qa.ld = ps->ld_qkv; qa.bq = L.bq; qa.bk = L.bk; qa.bv = L.bv;
+            qa.q_norm = m->qk_norm ? L.q_norm : nullptr; qa.k_norm = m->qk_norm ? L.k_norm : nullptr;
+            qa.rope = s->rope; qa.qr = ps->QR;
+            qa.kc = (char *)s->kc + (size_t)l * s->k_layer_elems * es;
+            qa.vc = (char *)s->vc + (size_t)l * s->v_layer_elems * es;
+            qa.nh = m->n_heads; qa.nkv = m->n_kv; qa.hd = hd; qa.ctx = s->ctx; qa.kstride = s->kstride;
+            qa.neox = m->rope_neox; qa.start = st0; qa.eps = m->eps;
+            const dim3 qgrid((unsigned)nc, (unsigned)(m->n_heads + m->n_kv));
+            if (s->kv_fp16) pf_qkv_post_kernel<__half><<<qgrid, 256, 0, st>>>(qa);
+            else pf_qkv_post_kernel<float><<<qgrid, 256, 0, st>>>(qa);
+            CK(cudaGetLastError());
+            PfAttnArgs aa;
+            aa.qr = ps->QR; aa.kc = qa.kc; aa.vc = qa.vc; aa.xq = ps->XQ; aa.k_pad = ps->k_pad[PF_K_QD];
+            aa.xs = ps->XS; aa.n_pad = ps->n_pad; aa.nh = m->n_heads; aa.nkv = m->n_kv; aa.hd = hd;
+            aa.ctx = s->ctx; aa.kstride = s->kstride; aa.start = st0; aa.n = nc; aa.tq = tq; aa.p_cap = p_cap;
+            aa.ex = m->ex;
+            const dim3 agrid((unsigned)m->n_kv, (unsigned)((nc + tq - 1) / tq));
+            const size_t asmem = (size_t)tq * (m->n_heads / m->n_kv) * p_cap * 4;
+            if (s->kv_fp16) pf_attn_kernel<__half><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
+            else pf_attn_kernel<float><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
+            CK(cudaGetLastError());
+            if (launch_gemm(P.wo, ps->mapB[PF_K_QD], ps->XS, ps->n_pad, nc, ps->X, m->dim, true, err, m->n_sm, st))
+                return 1;
+            // feed-forward block
+            ta.x = ps->X; ta.ld_x = m->dim; ta.norm_w = L.ffn_norm; ta.cols = m->dim; ta.k_pad = ps->k_pad[PF_K_DIM];
+            pf_norm_quant_kernel<<<nc, 256, (size_t)m->dim * 4, st>>>(ta);
+            CK(cudaGetLastError());
+            if (launch_gemm(P.w13, ps->mapB[PF_K_DIM], ps->XS, ps->n_pad, nc, ps->H, ps->ld_h, false, err,
+                            m->n_sm, st))
+                return 1;
+            ta.x = ps->H; ta.ld_x = ps->ld_h; ta.norm_w = nullptr; ta.cols = m->hidden; ta.hidden = m->hidden;
+            ta.k_pad = ps->k_pad[PF_K_HID];
+            pf_swiglu_quant_kernel<<<nc, 256, (size_t)m->hidden * 4, st>>>(ta);
+            CK(cudaGetLastError());
+            if (launch_gemm(P.w2, ps->mapB[PF_K_HID], ps->XS, ps->n_pad, nc, ps->X, m->dim, true, err, m->n_sm, st))
+                return 1;
+        }
+    }
+    // the last token's residual stream feeds the final norm + lm_head
+    CK(cudaMemcpyAsync(s->x, ps->X + (size_t)(nc - 1) * m->dim, (size_t)m->dim * 4, cudaMemcpyDeviceToDevice, st));
+    return 0;
+}
+
+// ------------------------------------------------------------ op level --------
+
+__global__ void __launch_bounds__(256) pf_quant_kernel(const PfTokArgs a) {
+    extern __shared__ __align__(16) float pf_row[];
+    const int t = blockIdx.x;
+    for (int i = threadIdx.x; i < a.cols; i += blockDim.x) pf_row[i] = a.x[(size_t)t * a.ld_x + i];
+    __syncthreads();
+    pf_quant_row(pf_row, a, t);
+}
+
+int pf_matmul_batch(int device, float *out, const float *x, const DevMat &w, int B, void *xq_blocks) {
+    if (pf_init(device)) return 1;
+    if (w.dtype != EMBER_DT_Q8_0 && w.dtype != EMBER_DT_Q4_0) return set_err("pf_matmul_batch: dtype");
+    PfModel pm;
+    PfMat pk;
+    const DevMat *parts[1] = { &w };
+    int rc = build_pack(&pm, &pk, parts, 1);
+    const int n_pad = (int)round_up((size_t)B, 128);
+    float *dx = nullptr, *dout = nullptr, *dxs = nullptr;
+    int8_t *dxq = nullptr;
+    int *derr = nullptr;
+    CUtensorMap maps[3];
+    std::vector<void *> tmp;
+    if (!rc) rc = pf_alloc(tmp, (void **)&dx, (size_t)B * w.cols * 4) || pf_alloc(tmp, (void **)&dout, (size_t)B * w.rows * 4) ||
+                  pf_alloc(tmp, (void **)&dxq, (size_t)n_pad * pk.k_pad) ||
+                  pf_alloc(tmp, (void **)&dxs, (size_t)pk.nb * n_pad * 4) || pf_alloc(tmp, (void **)&derr, 16);
+    if (!rc && (cudaMemset(dxq, 0, (size_t)n_pad * pk.k_pad) != cudaSuccess || cudaMemset(derr, 0, 16) != cudaSuccess ||
+                cudaMemset(dxs, 0, (size_t)pk.nb * n_pad * 4) != cudaSuccess ||
+                cudaMemcpy(dx, x, (size_t)B * w.cols * 4, cudaMemcpyHostToDevice) != cudaSuccess))
+        rc = set_err("pf_matmul_batch: upload failed");
+    for (int j = 0; j < 3 && !rc; j++) rc = map_i8(&maps[j], dxq, (size_t)pk.k_pad, (size_t)n_pad, PF_BNS[j]);
+    int nsm = 148;
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
+    if (!rc) {
+        PfTokArgs ta;
+        memset(&ta, 0, sizeof(ta));
+        ta.x = dx; ta.ld_x = w.cols; ta.cols = w.cols; ta.xq = dxq; ta.k_pad = pk.k_pad; ta.xs = dxs; ta.n_pad = n_pad;
+        pf_quant_kernel<<<B, 256, (size_t)w.cols * 4>>>(ta);
+        if (cudaGetLastError() != cudaSuccess) rc = set_err("pf_matmul_batch: quant launch failed");
+    }
+    if (!rc) rc = launch_gemm(pk, maps, dxs, n_pad, B, dout, w.rows, false, derr, nsm, 0);
+    int herr = 0;
+    if (!rc && (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpy(&herr, derr, 4, cudaMemcpyDeviceToHost) != cudaSuccess))
+        rc = set_err("pf_matmul_batch: %s", cudaGetErrorString(cudaGetLastError()));
+    if (!rc && herr) rc = set_err("pf_matmul_batch: device wait timed out (code %d)", herr);
+    if (!rc && cudaMemcpy(out, dout, (size_t)B * w.rows * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = set_err("pf_matmul_batch: download failed");
+    if (!rc && xq_blocks) {
+        // the caller's scratch receives the Q8_0 blocks of every column, as the
+        // reference's ember_matmul_batch leaves them (ref src/kernels.c:254-257)
+        const int nb = w.cols / 32;
+        std::vector<int8_t> hq((size_t)B * pk.k_pad);
+        std::vector<float> hs((size_t)nb * n_pad);
+        if (cudaMemcpy(hq.data(), dxq, hq.size(), cudaMemcpyDeviceToHost) != cudaSuccess ||
+            cudaMemcpy(hs.data(), dxs, hs.size() * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+            rc = set_err("pf_matmul_batch: download failed");
+        BlockQ8_0 *blk = static_cast<BlockQ8_0 *>(xq_blocks);
+        for (int b = 0; !rc && b < B; b++)
+            for (int j = 0; j < nb; j++) {
+                BlockQ8_0 &o = blk[(size_t)b * nb + j];
+                o.d = ember_f32_to_f16(hs[(size_t)j * n_pad + b]);   // exact: the value is an fp16
+                memcpy(o.qs, hq.data() + (size_t)b * pk.k_pad + (size_t)j * 32, 32);
+            }
+    }
+    for (void *p : tmp) cudaFree(p);
+    for (void *p : pm.allocs) cudaFree(p);
+    return rc;
+}
+
+}  // namespace emb

@@ -29,6 +29,7 @@
 #include "ember_cuda.h"
 #include "ember_ops.h"
 #include "kernels.cuh"
+#include "runtime_internal.cuh"
 
 using namespace emb;
 
@@ -36,20 +37,15 @@ using namespace emb;
 
 static char g_err[512] = "no error";
 
-static int set_err(const char *fmt, ...) {
+namespace emb {
+int set_err(const char *fmt, ...) {
     va_list ap;
     va_start(ap, fmt);
     vsnprintf(g_err, sizeof(g_err), fmt, ap);
     va_end(ap);
     return 1;
 }
-
-#define CK(call)                                                                           \
-    do {                                                                                   \
-        cudaError_t e_ = (call);                                                           \
-        if (e_ != cudaSuccess)                                                             \
-            return set_err("%s (%s:%d: %s)", cudaGetErrorString(e_), __FILE__, __LINE__, #call); \
-    } while (0)
+}  // namespace emb
 
 extern "C" const char *ember_cuda_error(void) { return g_err; }
 
@@ -102,38 +98,6 @@ static int init_kernel_attrs(int device) {
 
 // ------------------------------------------------------------------ model -----
 
-struct DevMat {
-    int dtype = EMBER_DT_F32, rows = 0, cols = 0;
-    uint8_t *q = nullptr;
-    __half *s = nullptr;
-};
-
-struct DevLayer {
-    DevMat wq, wk, wv, wo, w1, w2, w3;
-    float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
-    float *bq = nullptr, *bk = nullptr, *bv = nullptr;
-};
-
-struct EmberCudaModel {
-    int device = 0, n_sm = 148;
-    int dim = 0, hidden = 0, n_layers = 0, n_heads = 0, n_kv = 0, head_dim = 0, vocab = 0;
-    int qk_norm = 0, rope_neox = 0;
-    float eps = 0;
-    DevMat tok_emb, lm_head;
-    float *final_norm = nullptr;
-    std::vector<DevLayer> layers;
-    ExpfDev ex;
-    std::vector<void *> allocs;
-    uint64_t bytes = 0;
-};
-
-static int dalloc(EmberCudaModel *m, void **p, size_t n) {
-    CK(cudaMalloc(p, n ? n : 16));
-    m->allocs.push_back(*p);
-    m->bytes += n;
-    return 0;
-}
-
 static int upload_vec(EmberCudaModel *m, float **dst, const float *src, int n) {
     if (!src) { *dst = nullptr; return 0; }
     if (dalloc(m, (void **)dst, (size_t)n * 4)) return 1;
@@ -178,6 +142,7 @@ static int upload_mat(EmberCudaModel *m, DevMat *d, const EmberCudaMat &h) {
 }
 
 static void model_release(EmberCudaModel *m) {
+    pf_model_release(m);
     for (void *p : m->allocs) cudaFree(p);
     m->allocs.clear();
 }
@@ -243,40 +208,8 @@ extern "C" uint64_t ember_cuda_model_bytes(const EmberCudaModel *m) { return m ?
 
 // ------------------------------------------------------------------ state -----
 
-struct EmberCudaState {
-    EmberCudaModel *m = nullptr;
-    int ctx = 0, kv_fp16 = 0, kstride = 0;
-    cudaStream_t stream = nullptr;
-    std::vector<void *> allocs;
-    // device buffers
-    float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr;
-    float *od = nullptr, *of = nullptr, *hd = nullptr, *hf = nullptr, *logits = nullptr;
-    int8_t *oq = nullptr, *hq = nullptr;
-    void *kc = nullptr, *vc = nullptr;
-    size_t k_layer_elems = 0, v_layer_elems = 0;
-    float2 *rope = nullptr;
-    int *ctl = nullptr, *ids = nullptr, *out_tokens = nullptr;
-    float *am_v = nullptr;
-    int *am_i = nullptr;
-    unsigned *am_ticket = nullptr;
-    int am_blocks = 0;
-    int att_in_smem = 0, attn_chunk = 0;
-    size_t attn_smem = 0;
-    // pinned host
-    float *h_logits = nullptr;
-    int *h_ctl = nullptr;
-    // graphs
-    cudaGraphExec_t g_fwd = nullptr, g_greedy = nullptr, g_prefill = nullptr, g_head = nullptr;
-    int launches_per_step = 0;
-};
-
-static int salloc(EmberCudaState *s, void **p, size_t n) {
-    CK(cudaMalloc(p, n ? n : 16));
-    s->allocs.push_back(*p);
-    return 0;
-}
-
 static void state_release(EmberCudaState *s) {
+    pf_state_release(s);
     if (s->g_fwd) cudaGraphExecDestroy(s->g_fwd);
     if (s->g_greedy) cudaGraphExecDestroy(s->g_greedy);
     if (s->g_prefill) cudaGraphExecDestroy(s->g_prefill);
@@ -710,17 +643,32 @@ static int read_error_word(EmberCudaState *s) {
     return check_device_error(s, err);
 }
 
+// EMBER_PREFILL=steps runs every prefill as single-token steps (for comparisons)
+static bool batched_prefill_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("EMBER_PREFILL");
+        v = (e && strcmp(e, "steps") == 0) ? 0 : 1;
+    }
+    return v == 1;
+}
+
 extern "C" int ember_cuda_prefill(EmberCudaState *s, const int *ids, int n, int start, float *host_logits) {
     CK(cudaSetDevice(s->m->device));
     if (n <= 0) return 0;
-    if (!s->g_prefill && capture(s, &s->g_prefill, 2)) return 1;
     if (!s->g_head && capture(s, &s->g_head, 3)) return 1;
     int *hc = s->h_ctl;
     CK(cudaStreamSynchronize(s->stream));
     hc[CTL_POS] = start; hc[CTL_TOK] = 0; hc[CTL_NOUT] = 0; hc[CTL_BASE] = start; hc[CTL_ERR] = 0;
     CK(cudaMemcpyAsync(s->ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, s->stream));
     CK(cudaMemcpyAsync(s->ctl, hc, 5 * sizeof(int), cudaMemcpyHostToDevice, s->stream));
-    for (int i = 0; i < n; i++) CK(cudaGraphLaunch(s->g_prefill, s->stream));
+    if (n > 1 && batched_prefill_enabled() && pf_supported(s->m)) {
+        // all layers over the n tokens at once (tensor-core GEMMs), then the head
+        if (pf_run_layers(s, s->ids, n, start)) return 1;
+    } else {
+        if (!s->g_prefill && capture(s, &s->g_prefill, 2)) return 1;
+        for (int i = 0; i < n; i++) CK(cudaGraphLaunch(s->g_prefill, s->stream));
+    }
     CK(cudaGraphLaunch(s->g_head, s->stream));
     CK(cudaStreamSynchronize(s->stream));
     if (read_error_word(s)) return 1;
@@ -897,10 +845,29 @@ extern "C" void ember_matmul(float *out, const float *x, const void *w, int dtyp
     if (op_matmul(out, x, w, dtype, n_in, d_out, 1, xq)) ember_die("cuda: %s", g_err);
 }
 
+// quantized weights, two or more columns: the tensor-core GEMM of the batched
+// prefill (ref src/kernels.c:227-264); otherwise one GEMV per column
+static int op_matmul_batch(float *out, const float *x, const void *w, int dtype, int n_in, int d_out, int B,
+                           BlockQ8_0 *xq) {
+    int dev;
+    if (pick_device(&dev)) return 1;
+    if (n_in % 32) return set_err("ember_matmul_batch: n_in %% 32 != 0");
+    EmberCudaModel tmp;
+    tmp.device = dev;
+    DevMat dm;
+    EmberCudaMat hm = { w, dtype, d_out, n_in };
+    int rc = upload_mat(&tmp, &dm, hm);
+    if (!rc) rc = pf_matmul_batch(dev, out, x, dm, B, xq);
+    model_release(&tmp);
+    return rc;
+}
+
 extern "C" void ember_matmul_batch(float *out, const float *x, const void *w, int dtype, int n_in, int d_out,
                                    int B, BlockQ8_0 *xq) {
     if (B <= 0) return;
-    if (op_matmul(out, x, w, dtype, n_in, d_out, B, xq)) ember_die("cuda: %s", g_err);
+    const bool gemm = B > 1 && (dtype == EMBER_DT_Q8_0 || dtype == EMBER_DT_Q4_0) && batched_prefill_enabled();
+    if (gemm ? op_matmul_batch(out, x, w, dtype, n_in, d_out, B, xq) : op_matmul(out, x, w, dtype, n_in, d_out, B, xq))
+        ember_die("cuda: %s", g_err);
 }
 
 #ifdef EMBER_PROBES

@@ -58,6 +58,10 @@ CONFIGS = {
                          vocab_size=320, max_seq_len=256, rope_theta=100000.0, norm_eps=1e-5,
                          rope_style=ROPE_NEOX, tied=True, qk_norm=False, bias=False,
                          quant="q4_0"),
+    # long contexts: batched prefill in several chunks and softmax sums past 2048 terms
+    "tiny-long": dict(dim=128, hidden_dim=256, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=64,
+                      vocab_size=512, max_seq_len=4096, rope_theta=1e6, norm_eps=1e-6,
+                      rope_style=ROPE_NEOX, tied=True, qk_norm=True, bias=False, quant="q8_0"),
     "tiny-f32": dict(dim=64, hidden_dim=160, n_layers=2, n_heads=2, n_kv_heads=2, head_dim=32,
                      vocab_size=256, max_seq_len=128, rope_theta=10000.0, norm_eps=1e-5,
                      rope_style=ROPE_INTERLEAVED, tied=False, qk_norm=False, bias=False,
