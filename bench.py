@@ -55,6 +55,8 @@ def parse():
     p.add_argument("--cpu-baseline", type=int, default=1)
     p.add_argument("--prefill-tokens", type=int, default=512,
                    help="prompt length of the timed batched prefill (the reference's pp512)")
+    p.add_argument("--prefill-only", action="store_true",
+                   help="time only the batched prefill (NVTX range 'prefill' with --nvtx)")
     p.add_argument("--nvtx", action="store_true",
                    help="mark the timed region (and --kernel-case launches) as NVTX ranges "
                         "'timed' / 'case' for ncu --nvtx-include")
@@ -249,6 +251,30 @@ def max_over_ranks(dist, value):
 
 # ------------------------------------------------------------------ arms ------
 
+def time_prefill(args, lib, path, vocab, dist, nvtx):
+    """Batched prefill of a --prefill-tokens prompt (the reference's ppN): one
+    untimed call (builds the weight packs), then 3 timed calls, CUDA events on
+    the state's stream; seconds per prefill, max over ranks."""
+    import numpy as np
+    from emberllm_b200 import Ember
+    npf = args.prefill_tokens
+    ep = Ember(path, ctx=npf + 8)
+    csp = lib.ember_state_cuda(ep.st)
+    pprompt = [int(t) for t in np.random.default_rng(2).integers(0, vocab, npf)]
+    ep.prefill(pprompt)
+    barrier(dist)
+    nvtx.push("prefill")
+    lib.ember_cuda_mark(csp, 4)
+    for _ in range(3):
+        ep.prefill(pprompt)
+    lib.ember_cuda_mark(csp, 5)
+    nvtx.pop()
+    ms = ctypes.c_float()
+    assert lib.ember_cuda_elapsed_ms(csp, 4, 5, ctypes.byref(ms)) == 0, lib.ember_cuda_error()
+    ep.close()
+    return max_over_ranks(dist, ms.value / 1e3 / 3)
+
+
 def run_ours(args, world, rank, local, dist):
     import numpy as np
     from emberllm_b200 import Ember, load, synth
@@ -270,9 +296,13 @@ def run_ours(args, world, rank, local, dist):
         getattr(lib, name).argtypes = argt
 
     depth, ntok = args.depth, args.tokens
+    nvtx = Nvtx(args.nvtx)
+    if args.prefill_only:
+        s_pf = time_prefill(args, lib, path, cfg["vocab_size"], dist, nvtx)
+        return {"prefill_case": args.config, "tokens": args.prefill_tokens,
+                "ms": round(s_pf * 1e3, 3), "prefill_tok_s": round(args.prefill_tokens / s_pf, 1)}
     e = Ember(path, ctx=depth + ntok + 8)
     cs = lib.ember_state_cuda(e.st)
-    nvtx = Nvtx(args.nvtx)
     # kernels are timed alone at the step's mean position (attention length)
     kpos = depth + ntok // 2
     if args.kernel_case >= 0:
@@ -325,22 +355,8 @@ def run_ours(args, world, rank, local, dist):
     lib.ember_cuda_mark(cs, 3)
     t_e2e = max_over_ranks(dist, elapsed(2, 3))
 
-    # batched prefill of a --prefill-tokens prompt (the reference's ppN): one
-    # untimed call (builds the weight packs), then 3 timed calls on the stream
     npf = args.prefill_tokens
-    ep = Ember(path, ctx=npf + 8)
-    csp = lib.ember_state_cuda(ep.st)
-    pprompt = [int(t) for t in np.random.default_rng(2).integers(0, e.vocab, npf)]
-    ep.prefill(pprompt)
-    barrier(dist)
-    lib.ember_cuda_mark(csp, 4)
-    for _ in range(3):
-        ep.prefill(pprompt)
-    lib.ember_cuda_mark(csp, 5)
-    ms = ctypes.c_float()
-    assert lib.ember_cuda_elapsed_ms(csp, 4, 5, ctypes.byref(ms)) == 0, lib.ember_cuda_error()
-    prefill_s = max_over_ranks(dist, ms.value / 1e3 / 3)
-    ep.close()
+    prefill_s = time_prefill(args, lib, path, e.vocab, dist, nvtx)
 
     # roofline of the dominant kernel kind, timed live at kpos (overwrites the state)
     e.forward(0, kpos)

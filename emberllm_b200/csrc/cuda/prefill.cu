@@ -32,7 +32,9 @@
 namespace emb {
 
 constexpr int PF_CHUNK = 512;              // tokens per batched pass
-constexpr int PF_BNS[3] = { 32, 64, 128 };
+// token-tile widths of the GEMM: BN = 32 and 64 run two CTAs per SM, BN = 128 one
+constexpr int PF_NBN = 3;
+constexpr int PF_BNS[PF_NBN] = { 32, 64, 128 };
 
 static size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
 
@@ -214,7 +216,7 @@ struct PfState {
     float *X = nullptr, *XS = nullptr, *QKV = nullptr, *QR = nullptr, *H = nullptr;
     int8_t *XQ = nullptr;
     int ld_qkv = 0, ld_h = 0;
-    CUtensorMap mapB[3][3];    // [K kind][BN index]
+    CUtensorMap mapB[3][PF_NBN];    // [K kind][BN index]
     std::vector<void *> allocs;
 };
 
@@ -247,7 +249,7 @@ static int pf_prepare_state(EmberCudaState *s) {
                 cudaMemset(ps->XS, 0, (size_t)nbmax * ps->n_pad * 4) != cudaSuccess))
         rc = set_err("prefill scratch initialisation failed");
     for (int i = 0; i < 3 && !rc; i++)
-        for (int j = 0; j < 3 && !rc; j++)
+        for (int j = 0; j < PF_NBN && !rc; j++)
             rc = map_i8(&ps->mapB[i][j], ps->XQ, (size_t)ps->k_pad[i], (size_t)ps->n_pad, PF_BNS[j]);
     if (rc) {
         for (void *p : ps->allocs) cudaFree(p);
@@ -267,18 +269,20 @@ void pf_state_release(EmberCudaState *s) {
 
 // ------------------------------------------------------------ launches -------
 
-// Token-tile width: the one that minimises the busiest SM's share of tile-
-// columns (the epilogue's fp32 work grows with the width), counting the CTAs
-// each SM holds at once.
+// Token-tile width: the one that minimises the busiest SM's share of the
+// epilogue's fp32 work (tiles per SM x width); ties go to the narrow tile,
+// which spreads over more SMs and runs two CTAs per SM.
 static int choose_bn(int rows_pad, int n, int n_sm) {
-    int best = 2;
+    const char *force = getenv("EMBER_PF_BN");      // tuning: force a width
+    if (force && *force)
+        for (int j = 0; j < PF_NBN; j++)
+            if (atoi(force) == PF_BNS[j]) return j;
+    int best = 0;
     long long best_cost = -1;
-    for (int j = 2; j >= 0; j--) {
+    for (int j = 0; j < PF_NBN; j++) {
         const int bn = PF_BNS[j];
-        const int occ = bn == 128 ? 1 : 2;
         const long long tiles = (long long)(rows_pad / PF_BM) * ((n + bn - 1) / bn);
-        const long long waves = (tiles + (long long)n_sm * occ - 1) / ((long long)n_sm * occ);
-        const long long cost = waves * occ * bn;
+        const long long cost = (tiles + n_sm - 1) / n_sm * bn;
         if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = j; }
     }
     return best;
@@ -292,7 +296,7 @@ static int launch_gemm_bn(const PfMat &w, const CUtensorMap &mb, const PfGemmArg
     return 0;
 }
 
-static int launch_gemm(const PfMat &w, const CUtensorMap (&maps)[3], const float *xs, int n_pad, int n,
+static int launch_gemm(const PfMat &w, const CUtensorMap (&maps)[PF_NBN], const float *xs, int n_pad, int n,
                        float *out, int ld, bool resid, int *err, int n_sm, cudaStream_t st) {
     PfGemmArgs a;
     a.ws = w.s; a.xs = xs; a.out = out; a.err = err;
@@ -309,12 +313,25 @@ static int launch_gemm(const PfMat &w, const CUtensorMap (&maps)[3], const float
 }
 
 // attention tile: tokens per CTA so that rows * positions fit shared memory
-static int attn_tile(const EmberCudaModel *m, int p_cap, int *tq) {
+// attention tile: the most tokens per CTA (rows = tokens x kv_mul <= 16) whose
+// weights [positions][rows rounded up to 4] fit shared memory; 0 if none does
+static int attn_tile(const EmberCudaModel *m, int p_cap, int *tq, int *rs) {
     const int kv_mul = m->n_heads / m->n_kv;
-    int t = PF_ATT_MAX_ROWS / kv_mul;
-    while (t > 0 && (size_t)t * kv_mul * p_cap * 4 > (size_t)g_att_smem_cap) t--;
-    *tq = t;
-    return t > 0;
+    for (int t = PF_ATT_MAX_ROWS / kv_mul; t > 0; t--) {
+        const int r = (t * kv_mul + 3) / 4 * 4;
+        if (pf_attn_smem(p_cap, r) <= (size_t)g_att_smem_cap) {
+            *tq = t;
+            *rs = r;
+            return 1;
+        }
+    }
+    return 0;
+}
+
+int pf_fits(EmberCudaState *s, int n, int start) {
+    if (pf_init(s->m->device)) return 0;
+    int tq, rs;
+    return attn_tile(s->m, (int)round_up((size_t)(start + n), 4), &tq, &rs);
 }
 
 int pf_run_layers(EmberCudaState *s, const int *ids_dev, int n, int start) {
@@ -325,9 +342,9 @@ int pf_run_layers(EmberCudaState *s, const int *ids_dev, int n, int start) {
     int *err = s->ctl + CTL_ERR;
     const int hd = m->head_dim, qd = m->n_heads * hd;
     const size_t es = s->kv_fp16 ? 2 : 4;
-    int tq = 0;
+    int tq = 0, rs = 0;
     const int p_cap = (int)round_up((size_t)(start + n), 4);
-    if (!attn_tile(m, p_cap, &tq)) return set_err("prefill: %d positions do not fit the attention tile", start + n);
+    if (!attn_tile(m, p_cap, &tq, &rs)) return set_err("prefill: %d positions do not fit the attention tile", start + n);
     int nc = 0;
     for (int c0 = 0; c0 < n; c0 += ps->n_cap) {
         nc = n - c0 < ps->n_cap ? n - c0 : ps->n_cap;
@@ -367,10 +384,10 @@ int pf_run_layers(EmberCudaState *s, const int *ids_dev, int n, int start) {
             PfAttnArgs aa;
             aa.qr = ps->QR; aa.kc = qa.kc; aa.vc = qa.vc; aa.xq = ps->XQ; aa.k_pad = ps->k_pad[PF_K_QD];
             aa.xs = ps->XS; aa.n_pad = ps->n_pad; aa.nh = m->n_heads; aa.nkv = m->n_kv; aa.hd = hd;
-            aa.ctx = s->ctx; aa.kstride = s->kstride; aa.start = st0; aa.n = nc; aa.tq = tq; aa.p_cap = p_cap;
+            aa.ctx = s->ctx; aa.kstride = s->kstride; aa.start = st0; aa.n = nc; aa.tq = tq; aa.rs = rs; aa.p_cap = p_cap;
             aa.ex = m->ex;
             const dim3 agrid((unsigned)m->n_kv, (unsigned)((nc + tq - 1) / tq));
-            const size_t asmem = (size_t)tq * (m->n_heads / m->n_kv) * p_cap * 4;
+            const size_t asmem = pf_attn_smem(p_cap, rs);
             if (s->kv_fp16) pf_attn_kernel<__half><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
             else pf_attn_kernel<float><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
             CK(cudaGetLastError());
@@ -417,7 +434,7 @@ int pf_matmul_batch(int device, float *out, const float *x, const DevMat &w, int
     float *dx = nullptr, *dout = nullptr, *dxs = nullptr;
     int8_t *dxq = nullptr;
     int *derr = nullptr;
-    CUtensorMap maps[3];
+    CUtensorMap maps[PF_NBN];
     std::vector<void *> tmp;
     if (!rc) rc = pf_alloc(tmp, (void **)&dx, (size_t)B * w.cols * 4) || pf_alloc(tmp, (void **)&dout, (size_t)B * w.rows * 4) ||
                   pf_alloc(tmp, (void **)&dxq, (size_t)n_pad * pk.k_pad) ||
@@ -426,7 +443,7 @@ int pf_matmul_batch(int device, float *out, const float *x, const DevMat &w, int
                 cudaMemset(dxs, 0, (size_t)pk.nb * n_pad * 4) != cudaSuccess ||
                 cudaMemcpy(dx, x, (size_t)B * w.cols * 4, cudaMemcpyHostToDevice) != cudaSuccess))
         rc = set_err("pf_matmul_batch: upload failed");
-    for (int j = 0; j < 3 && !rc; j++) rc = map_i8(&maps[j], dxq, (size_t)pk.k_pad, (size_t)n_pad, PF_BNS[j]);
+    for (int j = 0; j < PF_NBN && !rc; j++) rc = map_i8(&maps[j], dxq, (size_t)pk.k_pad, (size_t)n_pad, PF_BNS[j]);
     int nsm = 148;
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
     if (!rc) {
@@ -466,3 +483,12 @@ int pf_matmul_batch(int device, float *out, const float *x, const DevMat &w, int
 }
 
 }  // namespace emb
+
+#ifdef EMBER_PROBES
+// profiling build only: the last GEMM launch's trace (1024 timestamps)
+extern "C" int ember_cuda_pf_trace_read(unsigned long long *out, unsigned long long *cta) {
+    if (cudaDeviceSynchronize() != cudaSuccess) return 1;
+    if (cta && cudaMemcpyFromSymbol(cta, emb::g_pf_cta, sizeof(emb::g_pf_cta)) != cudaSuccess) return 1;
+    return cudaMemcpyFromSymbol(out, emb::g_pf_trace, sizeof(emb::g_pf_trace)) != cudaSuccess;
+}
+#endif

@@ -120,19 +120,21 @@ EMB_DEV void mma_commit(uint64_t *bar) {
                  : "memory");
 }
 
-// 32 consecutive 32-bit TMEM columns of this thread's lane; the wait is in the
-// same statement so no use of r[] can be scheduled before the data arrives
-EMB_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// 16 consecutive 32-bit TMEM columns of this thread's lane at two addresses
+// (r[0..15] from ta, r[16..31] from tb); the wait is in the same statement so
+// no use of r[] is scheduled before the data arrives
+EMB_DEV void tmem_ld16x2(uint32_t ta, uint32_t tb, uint32_t (&r)[32]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];\n\t"
         "tcgen05.wait::ld.sync.aligned;"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr)
+        : "r"(ta), "r"(tb)
         : "memory");
 }
 
@@ -166,6 +168,37 @@ EMB_DEV float2 mul_f32x2(float2 a, float2 b) {
 }
 
 // ------------------------------------------------------------------- GEMM ------
+
+// profiling build only (-DEMBER_PROBES): CTA (0,0) of the last GEMM launch
+// records when the producer issued each stage, the MMA warp each block, and
+// epilogue warp 0 the phases of each block pair. Timestamps only.
+#ifdef EMBER_PROBES
+__device__ unsigned long long g_pf_trace[1024];
+__device__ unsigned long long g_pf_cta[1024][3];   // per CTA: SM id, start, end
+EMB_DEV unsigned pf_smid() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+    return r;
+}
+#define PF_CTA_MARK(k)                                                                   \
+    do {                                                                                 \
+        const unsigned c_ = blockIdx.y * gridDim.x + blockIdx.x;                         \
+        if (threadIdx.x == 0 && c_ < 1024) {                                             \
+            if ((k) == 1) g_pf_cta[c_][0] = pf_smid();                                   \
+            g_pf_cta[c_][k] = probe_now();                                               \
+        }                                                                                \
+    } while (0)
+#else
+#define PF_CTA_MARK(k) do {} while (0)
+#endif
+#ifdef EMBER_PROBES
+#define PF_TRACE(idx)                                                                    \
+    do {                                                                                 \
+        if (blockIdx.x == 0 && blockIdx.y == 0 && (idx) < 1024) g_pf_trace[idx] = probe_now(); \
+    } while (0)
+#else
+#define PF_TRACE(idx) do {} while (0)
+#endif
 
 constexpr int PF_BM = 128;      // weight rows per tile (the MMA's M)
 constexpr int PF_BK = 128;      // K bytes per pipeline stage: four quant blocks
@@ -201,28 +234,38 @@ struct PfLayout {
     static constexpr int OFF_B = OFF_A + PF_STAGES * A_BYTES;
     static constexpr int OFF_XS = OFF_B + PF_STAGES * B_BYTES;
     static constexpr int OFF_BAR = OFF_XS + PF_STAGES * XS_BYTES;
-    static constexpr int N_BARS = 2 * PF_STAGES + 5;
+    // CTAs per SM: two for BN = 32 / 64 (83 / 101 KB of shared memory), one for
+    // BN = 128 (137 KB); the TMEM ring of block-pair accumulators fills the SM's
+    // 512 columns between them
+    static constexpr int MIN_CTAS = BN == 128 ? 1 : 2;
+    static constexpr int NPAIR = (512 / MIN_CTAS) / (2 * BN) > 4 ? 4 : (512 / MIN_CTAS) / (2 * BN);
+    static constexpr int N_BARS = 2 * PF_STAGES + 2 * NPAIR + 1;
     static constexpr int OFF_TMEM = OFF_BAR + N_BARS * 8;
     static constexpr int SMEM = OFF_TMEM + 16 + 1024;  // + slack to align the base to 1024
-    static constexpr uint32_t TMEM_COLS = 2 * BN;     // two accumulators
+    static constexpr uint32_t TMEM_COLS = 2 * NPAIR * BN;
 };
 
-// One CTA computes a 128-row x BN-token output tile over all K blocks.
+// One CTA computes a 128-row x BN-token output tile over all K blocks, the
+// blocks taken in pairs (one handshake per pair between the MMA warp and the
+// epilogue: each tcgen05 / mbarrier operation costs tens of cycles to issue).
 //   warp EW      (lane 0) TMA producer: per stage, a 128 x 128-byte weight box,
 //                a BN x 128-byte activation box (both 128-byte swizzled) and the
 //                activation scales of the stage's four blocks (bulk copies).
-//   warp EW + 1  TMEM allocator; (lane 0) MMA issuer: one kind::i8 MMA per quant
-//                block into accumulator b & 1, committed to acc_full.
+//   warp EW + 1  TMEM allocator; (lane 0) MMA issuer: per block pair, two
+//                kind::i8 MMAs (K = 32 each) into the pair's two accumulators,
+//                one commit to acc_full[pair slot].
 //   warps < EW   epilogue: warp w owns TMEM lanes 32*(w%4).. (tile rows) and
-//                columns 32*(w/4).. (tokens); per block it reads its 32 int32
-//                sums, frees the accumulator, and adds the block's terms.
+//                columns 32*(w/4).. (tokens); per pair it reads the two blocks'
+//                int32 sums 16 columns at a time, frees the pair slot, and adds
+//                the terms of block 2p then 2p+1 to each column's chain.
 // Every wait is bounded; a wait that gives up records ERR_PF_WAIT and the CTA
 // drains its copies and MMAs, frees its TMEM and exits.
 template <int BN, int EPI>
-__global__ void __launch_bounds__(PfLayout<BN>::THREADS) pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                                                                       const __grid_constant__ CUtensorMap tmB,
-                                                                       const PfGemmArgs a) {
+__global__ void __launch_bounds__(PfLayout<BN>::THREADS, PfLayout<BN>::MIN_CTAS)
+    pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const PfGemmArgs a) {
     using Lay = PfLayout<BN>;
+    constexpr int NP = Lay::NPAIR;
     extern __shared__ unsigned char pf_smem_raw[];
     __shared__ int abort_flag;
     const uint32_t raw = smem_u32(pf_smem_raw);
@@ -230,21 +273,22 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS) pf_gemm_kernel(const __
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + Lay::OFF_BAR);
     uint64_t *empty = full + PF_STAGES;
     uint64_t *accf = empty + PF_STAGES;
-    uint64_t *acce = accf + 2;
-    uint64_t *fin = acce + 2;
+    uint64_t *acce = accf + NP;
+    uint64_t *fin = acce + NP;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + Lay::OFF_TMEM);
     volatile int *abort_v = &abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * PF_BM, n0 = blockIdx.y * BN;
-    const int nb = a.nb, n_st = (nb + 3) / 4;
+    const int nb = a.nb, n_st = (nb + 3) / 4, n_pairs = (nb + 1) / 2;
+    PF_CTA_MARK(1);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < PF_STAGES; i++) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1 + Lay::EW);
         }
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < NP; i++) {
             mbar_init(&accf[i], 1);
             mbar_init(&acce[i], Lay::EW);
         }
@@ -269,6 +313,7 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS) pf_gemm_kernel(const __
                     break;
                 }
                 const int nblk = min(4, nb - 4 * st);
+                if (st < 128) PF_TRACE(st);
                 mbar_expect_tx(&full[slot], (uint32_t)(Lay::A_BYTES + Lay::B_BYTES + nblk * BN * 4));
                 tma_load_2d(sm + Lay::OFF_A + slot * Lay::A_BYTES, &tmA, st * PF_BK, m0, &full[slot]);
                 tma_load_2d(sm + Lay::OFF_B + slot * Lay::B_BYTES, &tmB, st * PF_BK, n0, &full[slot]);
@@ -288,22 +333,26 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS) pf_gemm_kernel(const __
                                    | (1u << 7) | (1u << 10)         // A, B: signed int8
                                    | ((uint32_t)(BN >> 3) << 17)    // N
                                    | ((uint32_t)(PF_BM >> 4) << 24);  // M
-            for (int b = 0; b < nb; b++) {
-                const int st = b >> 2, j = b & 3, slot = st % PF_STAGES, buf = b & 1;
-                if (j == 0 && !pf_wait(&full[slot], (uint32_t)((st / PF_STAGES) & 1), a.err, abort_v)) {
+            for (int p = 0; p < n_pairs; p++) {
+                const int st = p >> 1, slot = st % PF_STAGES, ps = p % NP;
+                if ((p & 1) == 0 && !pf_wait(&full[slot], (uint32_t)((st / PF_STAGES) & 1), a.err, abort_v)) {
                     *abort_v = 1;
                     break;
                 }
-                if (!pf_wait(&acce[buf], (uint32_t)(((b >> 1) & 1) ^ 1), a.err, abort_v)) {
+                if (!pf_wait(&acce[ps], (uint32_t)(((p / NP) & 1) ^ 1), a.err, abort_v)) {
                     *abort_v = 1;
                     break;
                 }
                 tc_fence_after();
-                const uint64_t ad = umma_desc_sw128(smem_u32(sm + Lay::OFF_A + slot * Lay::A_BYTES) + 32u * j);
-                const uint64_t bd = umma_desc_sw128(smem_u32(sm + Lay::OFF_B + slot * Lay::B_BYTES) + 32u * j);
-                mma_i8(tmem + (uint32_t)(buf * BN), ad, bd, idesc);
-                mma_commit(&accf[buf]);
-                if (j == 3 || b == nb - 1) mma_commit(&empty[slot]);
+                if (p < 64) PF_TRACE(128 + p);
+                const uint32_t sa = smem_u32(sm + Lay::OFF_A + slot * Lay::A_BYTES) + 64u * (p & 1);
+                const uint32_t sb = smem_u32(sm + Lay::OFF_B + slot * Lay::B_BYTES) + 64u * (p & 1);
+                mma_i8(tmem + (uint32_t)(2 * ps * BN), umma_desc_sw128(sa), umma_desc_sw128(sb), idesc);
+                if (2 * p + 1 < nb)
+                    mma_i8(tmem + (uint32_t)((2 * ps + 1) * BN), umma_desc_sw128(sa + 32u), umma_desc_sw128(sb + 32u),
+                           idesc);
+                mma_commit(&accf[ps]);
+                if ((p & 1) == 1 || p == n_pairs - 1) mma_commit(&empty[slot]);
             }
             // every MMA issued above has completed before TMEM is released
             mma_commit(fin);
@@ -319,45 +368,67 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS) pf_gemm_kernel(const __
 #pragma unroll
         for (int j = 0; j < 16; j++) s2[j] = make_float2(0.0f, 0.0f);
         const float2 magic = make_float2(PF_MAGIC_F, PF_MAGIC_F);
+        // this row's weight scales, four blocks per load, fetched one stage ahead
         float4 dw4 = *reinterpret_cast<const float4 *>(wsr);
-        for (int b = 0; b < nb; b++) {
-            const int buf = b & 1, st = b >> 2, slot = st % PF_STAGES;
+        float4 dw4n = a.nbp > 4 ? *reinterpret_cast<const float4 *>(wsr + 4) : dw4;
+        const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(cg * 32);
+        for (int p = 0; p < n_pairs; p++) {
+            const int st = p >> 1, slot = st % PF_STAGES, ps = p % NP;
+            const int b = 2 * p, two = b + 1 < nb;
+            const int tr = warp == 0 && lane == 0 && p < 160 ? 384 + 4 * p : 1024;
+            PF_TRACE(tr);
             // lane 0 waits, the warp follows it (tcgen05.ld needs the whole warp)
             int ok = 1;
-            if ((b & 3) == 0) {
-                if (b > 0) dw4 = *reinterpret_cast<const float4 *>(wsr + b);
+            if ((p & 1) == 0) {
+                if (p > 0) {
+                    dw4 = dw4n;
+                    if (b + 4 < a.nbp) dw4n = *reinterpret_cast<const float4 *>(wsr + b + 4);
+                }
                 // the stage's scale copies: observed by this warp too
                 if (lane == 0) ok = pf_wait(&full[slot], (uint32_t)((st / PF_STAGES) & 1), a.err, abort_v);
             }
-            if (lane == 0 && ok) ok = pf_wait(&accf[buf], (uint32_t)((b >> 1) & 1), a.err, abort_v);
+            if (lane == 0 && ok) ok = pf_wait(&accf[ps], (uint32_t)((p / NP) & 1), a.err, abort_v);
             if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            PF_TRACE(tr + 1);
             tc_fence_after();
-            uint32_t r[32];
-            tmem_ld32(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(buf * BN + cg * 32), r);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acce[buf]);
-            const float dw = (b & 3) == 0 ? dw4.x : (b & 3) == 1 ? dw4.y : (b & 3) == 2 ? dw4.z : dw4.w;
-            const float2 dw2 = make_float2(dw, dw);
-            const float4 *xsv = reinterpret_cast<const float4 *>(sm + Lay::OFF_XS + slot * Lay::XS_BYTES) +
+            const float dwa = (p & 1) ? dw4.z : dw4.x, dwb = (p & 1) ? dw4.w : dw4.y;
+            const float4 *xsa = reinterpret_cast<const float4 *>(sm + Lay::OFF_XS + slot * Lay::XS_BYTES) +
                                 ((b & 3) * BN + cg * 32) / 4;
+            const float4 *xsb = xsa + BN / 4;
 #pragma unroll
-            for (int q4 = 0; q4 < 8; q4++) {
-                const float4 xv = xsv[q4];
-                float2 f0 = make_float2(__int_as_float((int)r[4 * q4 + 0] + PF_MAGIC_I),
-                                        __int_as_float((int)r[4 * q4 + 1] + PF_MAGIC_I));
-                float2 f1 = make_float2(__int_as_float((int)r[4 * q4 + 2] + PF_MAGIC_I),
-                                        __int_as_float((int)r[4 * q4 + 3] + PF_MAGIC_I));
-                f0 = mul_f32x2(sub_f32x2(f0, magic), dw2);
-                f1 = mul_f32x2(sub_f32x2(f1, magic), dw2);
-                // the multiply whose result is added is scalar: ptxas may contract a
-                // packed mul.f32x2 feeding an add into an fma, a scalar mul.rn never
-                f0 = make_float2(fmul(f0.x, xv.x), fmul(f0.y, xv.y));
-                f1 = make_float2(fmul(f1.x, xv.z), fmul(f1.y, xv.w));
-                s2[2 * q4] = add_f32x2(s2[2 * q4], f0);
-                s2[2 * q4 + 1] = add_f32x2(s2[2 * q4 + 1], f1);
+            for (int h = 0; h < 2; h++) {
+                uint32_t r[32];
+                tmem_ld16x2(tl + (uint32_t)(2 * ps * BN + 16 * h), tl + (uint32_t)((2 * ps + 1) * BN + 16 * h), r);
+                if (h == 1) {
+                    // both halves read: the pair slot is free for the MMA warp
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acce[ps]);
+                }
+#pragma unroll
+                for (int blk = 0; blk < 2; blk++) {
+                    if (blk == 1 && !two) break;
+                    const float2 dw2 = blk ? make_float2(dwb, dwb) : make_float2(dwa, dwa);
+                    const float4 *xsv = (blk ? xsb : xsa) + 4 * h;
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; q4++) {
+                        const float4 xv = xsv[q4];
+                        const uint32_t *rr = r + 16 * blk + 4 * q4;
+                        float2 f0 = make_float2(__int_as_float((int)rr[0] + PF_MAGIC_I), __int_as_float((int)rr[1] + PF_MAGIC_I));
+                        float2 f1 = make_float2(__int_as_float((int)rr[2] + PF_MAGIC_I), __int_as_float((int)rr[3] + PF_MAGIC_I));
+                        f0 = mul_f32x2(sub_f32x2(f0, magic), dw2);
+                        f1 = mul_f32x2(sub_f32x2(f1, magic), dw2);
+                        // the multiply whose result is added is scalar: ptxas may contract a
+                        // packed mul.f32x2 feeding an add into an fma, a scalar mul.rn never
+                        f0 = make_float2(fmul(f0.x, xv.x), fmul(f0.y, xv.y));
+                        f1 = make_float2(fmul(f1.x, xv.z), fmul(f1.y, xv.w));
+                        s2[8 * h + 2 * q4] = add_f32x2(s2[8 * h + 2 * q4], f0);
+                        s2[8 * h + 2 * q4 + 1] = add_f32x2(s2[8 * h + 2 * q4 + 1], f1);
+                    }
+                }
             }
-            if ((b & 3) == 3 || b == nb - 1) {
+            PF_TRACE(tr + 3);
+            if ((p & 1) == 1 || p == n_pairs - 1) {
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[slot]);
             }
@@ -380,6 +451,7 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS) pf_gemm_kernel(const __
         tc_fence_after();
         tmem_dealloc(tmem, Lay::TMEM_COLS);
     }
+    PF_CTA_MARK(2);
 }
 
 // --------------------------------------------------------------- packing -------
@@ -576,7 +648,7 @@ __global__ void __launch_bounds__(256) pf_qkv_post_kernel(const PfQkvArgs a) {
 
 // ------------------------------------------------------------------ attention --
 
-constexpr int PF_ATT_THREADS = 128;
+constexpr int PF_ATT_THREADS = 256;
 constexpr int PF_ATT_MAX_ROWS = 16;
 
 struct PfAttnArgs {
@@ -588,73 +660,94 @@ struct PfAttnArgs {
     int n_pad;
     int nh, nkv, hd, ctx, kstride, start, n;
     int tq;                // tokens per CTA; rows = tq * (nh / nkv) <= PF_ATT_MAX_ROWS
-    int p_cap;             // score columns per row in shared memory
+    int rs;                // weight row stride: rows rounded up to 4
+    int p_cap;             // positions held in shared memory (>= start + n)
     ExpfDev ex;
 };
 
+// shared memory of one attention CTA: the weights [p_cap][rs] and, when a row
+// has more than 2048 positions, one contiguous row for the exact parallel sum
+__host__ __device__ inline size_t pf_attn_smem(int p_cap, int rs) {
+    return (size_t)p_cap * rs * 4 + (p_cap > 2048 ? (size_t)p_cap * 4 : 0);
+}
+
 // One CTA per (kv head, tile of tq consecutive tokens); its query rows are the
-// tile's tokens x the kv head's query heads. Token j of the tile attends to
-// positions 0..start+b0+j. For every row, as in the single-token step (ref
-// src/model.c:221-259):
-//   scores   sc_t = sum_i q_i*k_t,i in index order, * (1/sqrt(hd));
+// tile's tokens x the kv head's query heads (row r = token r / kv_mul, head
+// kvh * kv_mul + r % kv_mul). Token j attends to positions 0..start+b0+j. For
+// every row, as in the single-token step (ref src/model.c:221-259):
+//   scores   sc_t = sum_i q_i*k_t,i in index order, * (1/sqrt(hd)) -- one thread
+//            per position, the 16 rows' chains side by side (each key element
+//            loaded once serves every row);
 //   softmax  max, e_t = expf(sc_t - max), den = sequential sum over t (CTA-
 //            parallel exact evaluation above 2048 terms), w_t = e_t * (1/den);
-//   output   o_i = sum_t w_t*v_t,i in position order, then quantized.
-// Each thread carries the chains of all rows at once, so every key and value
-// element it loads serves `rows` chains.
+//   output   o_i = sum_t w_t*v_t,i in position order -- one thread per
+//            (dimension, row group), then quantized per (token, head).
+// Weights sit in shared memory as [position][rs rows], so the output loop
+// reads four rows per load. Loads of keys and values run eight ahead of the
+// chains. Products are rounded by scalar multiplies and added in pairs
+// (add.f32x2): the same two roundings per step as the reference.
 template <typename T>
 __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArgs a) {
-    extern __shared__ __align__(16) float pf_att[];        // [rows][p_cap] scores / weights
-    __shared__ __align__(16) float q_s[256 * PF_ATT_MAX_ROWS];   // [hd][rows]
+    extern __shared__ __align__(16) float pf_att[];              // [p_cap][rs]
+    __shared__ __align__(16) float q_s[256 * PF_ATT_MAX_ROWS];   // [hd][16]
     __shared__ float red[PF_ATT_MAX_ROWS][PF_ATT_THREADS / 32];
     __shared__ float s_max[PF_ATT_MAX_ROWS], s_inv[PF_ATT_MAX_ROWS];
     __shared__ XsScratch xs;
+    constexpr int RS = PF_ATT_MAX_ROWS;   // q_s stride and register rows
+    const int rs = a.rs;                  // weight stride in shared memory (<= RS)
     const int kvh = blockIdx.x, b0 = blockIdx.y * a.tq, tid = threadIdx.x, hd = a.hd;
     const int kv_mul = a.nh / a.nkv;
     const int ntok = min(a.tq, a.n - b0);
     const int rows = ntok * kv_mul;
     const int qd = a.nh * hd;
-    const int p_last = a.start + b0 + ntok - 1;     // the tile's last position
+    const int p_first = a.start + b0;                // every row sees positions 0..p_first
+    const int p_last = a.start + b0 + ntok - 1;      // the tile's last position
     const T *kt = reinterpret_cast<const T *>(a.kc) + (size_t)kvh * hd * a.kstride;
     const T *vt = reinterpret_cast<const T *>(a.vc) + (size_t)kvh * a.ctx * hd;
-    // row r = token j * kv_mul + head hm  (query head kvh * kv_mul + hm)
-    for (int idx = tid; idx < PF_ATT_MAX_ROWS * hd; idx += PF_ATT_THREADS) {
+    float *row_buf = pf_att + (size_t)a.p_cap * rs;  // contiguous row for long sums
+    for (int idx = tid; idx < RS * hd; idx += PF_ATT_THREADS) {
         const int r = idx / hd, i = idx - r * hd;
         const int j = r / kv_mul, hm = r - j * kv_mul;
-        q_s[i * PF_ATT_MAX_ROWS + r] = r < rows ? a.qr[(size_t)(b0 + j) * qd + (kvh * kv_mul + hm) * hd + i] : 0.0f;
+        q_s[i * RS + r] = r < rows ? a.qr[(size_t)(b0 + j) * qd + (kvh * kv_mul + hm) * hd + i] : 0.0f;
     }
     __syncthreads();
 
     // ---- scores ----
     const float inv_sqrt = fdiv(1.0f, fsqrt((float)hd));
     for (int t = tid; t <= p_last; t += PF_ATT_THREADS) {
-        float sc[PF_ATT_MAX_ROWS];
+        float2 sc[RS / 2];
 #pragma unroll
-        for (int r = 0; r < PF_ATT_MAX_ROWS; r++) sc[r] = 0.0f;
-        for (int i = 0; i < hd; i++) {
-            const float k = widen(kt[(size_t)i * a.kstride + t]);
-            const float4 *qv = reinterpret_cast<const float4 *>(q_s + i * PF_ATT_MAX_ROWS);
+        for (int r = 0; r < RS / 2; r++) sc[r] = make_float2(0.0f, 0.0f);
+        for (int i = 0; i < hd; i += 8) {
+            float kk[8];
 #pragma unroll
-            for (int r4 = 0; r4 < PF_ATT_MAX_ROWS / 4; r4++) {
-                const float4 q4 = qv[r4];
-                sc[4 * r4 + 0] = fadd(sc[4 * r4 + 0], fmul(q4.x, k));
-                sc[4 * r4 + 1] = fadd(sc[4 * r4 + 1], fmul(q4.y, k));
-                sc[4 * r4 + 2] = fadd(sc[4 * r4 + 2], fmul(q4.z, k));
-                sc[4 * r4 + 3] = fadd(sc[4 * r4 + 3], fmul(q4.w, k));
+            for (int j = 0; j < 8; j++) kk[j] = widen(kt[(size_t)(i + j) * a.kstride + t]);
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const float4 *qv = reinterpret_cast<const float4 *>(q_s + (i + j) * RS);
+#pragma unroll
+                for (int r4 = 0; r4 < RS / 4; r4++) {
+                    const float4 q4 = qv[r4];
+                    sc[2 * r4] = add_f32x2(sc[2 * r4], make_float2(fmul(q4.x, kk[j]), fmul(q4.y, kk[j])));
+                    sc[2 * r4 + 1] = add_f32x2(sc[2 * r4 + 1], make_float2(fmul(q4.z, kk[j]), fmul(q4.w, kk[j])));
+                }
             }
         }
+        float4 *dst = reinterpret_cast<float4 *>(pf_att + (size_t)t * rs);
 #pragma unroll
-        for (int r = 0; r < PF_ATT_MAX_ROWS; r++)
-            if (r < rows) pf_att[(size_t)r * a.p_cap + t] = fmul(sc[r], inv_sqrt);
+        for (int r4 = 0; r4 < RS / 4; r4++)
+            if (4 * r4 < rs)
+                dst[r4] = make_float4(fmul(sc[2 * r4].x, inv_sqrt), fmul(sc[2 * r4].y, inv_sqrt),
+                                  fmul(sc[2 * r4 + 1].x, inv_sqrt), fmul(sc[2 * r4 + 1].y, inv_sqrt));
     }
     __syncthreads();
 
-    // ---- softmax, row by row for the reductions ----
+    // ---- softmax ----
     const int warp = tid >> 5, lane = tid & 31;
     for (int r = 0; r < rows; r++) {
         const int pr = a.start + b0 + r / kv_mul;   // this row's position
         float m = -INFINITY;
-        for (int t = tid; t <= pr; t += PF_ATT_THREADS) m = fmaxf(m, pf_att[(size_t)r * a.p_cap + t]);
+        for (int t = tid; t <= pr; t += PF_ATT_THREADS) m = fmaxf(m, pf_att[(size_t)t * rs + r]);
         m = warp_max(m);
         if (lane == 0) red[r][warp] = m;
     }
@@ -665,65 +758,106 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
         s_max[tid] = m;
     }
     __syncthreads();
-    for (int r = 0; r < rows; r++) {
-        const int pr = a.start + b0 + r / kv_mul;
-        const float mx = s_max[r];
-        float *ar = pf_att + (size_t)r * a.p_cap;
-        for (int t = tid; t <= pr; t += PF_ATT_THREADS) ar[t] = expf_exact(a.ex, fsub(ar[t], mx));
+    for (int idx = tid; idx < (p_last + 1) * rs; idx += PF_ATT_THREADS) {
+        const int t = idx / rs, r = idx - t * rs;
+        if (r < rows && t <= a.start + b0 + r / kv_mul) pf_att[idx] = expf_exact(a.ex, fsub(pf_att[idx], s_max[r]));
     }
     __syncthreads();
     // denominators: short sums as one chain per row (rows in parallel), long
-    // ones by the CTA-parallel exact evaluation, one row at a time
+    // ones by the CTA-parallel exact evaluation over a contiguous copy
     if (tid < rows) {
         const int pr = a.start + b0 + tid / kv_mul;
-        if (pr + 1 <= 2048) s_inv[tid] = fdiv(1.0f, chain_sum(0.0f, pf_att + (size_t)tid * a.p_cap, pr + 1));
+        if (pr + 1 <= 2048) {
+            float sum = 0.0f;
+            int t = 0;
+            for (; t + 8 <= pr + 1; t += 8) {
+                float e[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) e[j] = pf_att[(size_t)(t + j) * rs + tid];
+#pragma unroll
+                for (int j = 0; j < 8; j++) sum = fadd(sum, e[j]);
+            }
+            for (; t <= pr; t++) sum = fadd(sum, pf_att[(size_t)t * rs + tid]);
+            s_inv[tid] = fdiv(1.0f, sum);
+        }
     }
     for (int r = 0; r < rows; r++) {
         const int pr = a.start + b0 + r / kv_mul;
         if (pr + 1 > 2048) {
-            const float den = exact_pos_sum<PF_ATT_THREADS>(pf_att + (size_t)r * a.p_cap, pr + 1, &xs);
+            __syncthreads();
+            for (int t = tid; t <= pr; t += PF_ATT_THREADS) row_buf[t] = pf_att[(size_t)t * rs + r];
+            __syncthreads();
+            const float den = exact_pos_sum<PF_ATT_THREADS>(row_buf, pr + 1, &xs);
             if (tid == 0) s_inv[r] = fdiv(1.0f, den);
         }
     }
     __syncthreads();
-    for (int r = 0; r < rows; r++) {
-        const int pr = a.start + b0 + r / kv_mul;
-        const float inv = s_inv[r];
-        float *ar = pf_att + (size_t)r * a.p_cap;
-        for (int t = tid; t <= pr; t += PF_ATT_THREADS) ar[t] = fmul(ar[t], inv);
+    for (int idx = tid; idx < (p_last + 1) * rs; idx += PF_ATT_THREADS) {
+        const int t = idx / rs, r = idx - t * rs;
+        if (r < rows && t <= a.start + b0 + r / kv_mul) pf_att[idx] = fmul(pf_att[idx], s_inv[r]);
     }
     __syncthreads();
 
-    // ---- outputs: one thread per dimension (and per further 128 dimensions) ----
+    // ---- outputs: thread = (dimension, row group) ----
+    const int groups = hd >= PF_ATT_THREADS ? 1 : PF_ATT_THREADS / hd;   // 1, 2 or 4
+    const int rg = (rs + 4 * groups - 1) / (4 * groups) * 4;             // rows per group, a multiple of 4
     for (int i0 = 0; i0 < hd; i0 += PF_ATT_THREADS) {
-        const int i = i0 + tid;
-        float o[PF_ATT_MAX_ROWS];
+        const int g = groups > 1 ? tid / hd : 0;
+        const int i = groups > 1 ? tid - g * hd : i0 + tid;
+        const int r0 = g * rg;
+        float2 o[RS / 2];
 #pragma unroll
-        for (int r = 0; r < PF_ATT_MAX_ROWS; r++) o[r] = 0.0f;
-        if (i < hd) {
-            int pr[PF_ATT_MAX_ROWS];   // each row's last position (-1: no such row)
+        for (int r = 0; r < RS / 2; r++) o[r] = make_float2(0.0f, 0.0f);
+        if (i < hd && r0 < rows) {
+            // positions every row takes
+            int t = 0;
+            for (; t + 8 <= p_first + 1; t += 8) {
+                float vv[8];
 #pragma unroll
-            for (int r = 0; r < PF_ATT_MAX_ROWS; r++) pr[r] = r < rows ? a.start + b0 + r / kv_mul : -1;
-            for (int t = 0; t <= p_last; t++) {
+                for (int j = 0; j < 8; j++) vv[j] = widen(vt[(size_t)(t + j) * hd + i]);
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const float4 *wv = reinterpret_cast<const float4 *>(pf_att + (size_t)(t + j) * rs + r0);
+#pragma unroll
+                    for (int r4 = 0; r4 < RS / 4; r4++) {
+                        if (4 * r4 < rg && r0 + 4 * r4 < rs) {   // stay inside this position's row
+                            const float4 w4 = wv[r4];
+                            o[2 * r4] = add_f32x2(o[2 * r4], make_float2(fmul(w4.x, vv[j]), fmul(w4.y, vv[j])));
+                            o[2 * r4 + 1] = add_f32x2(o[2 * r4 + 1], make_float2(fmul(w4.z, vv[j]), fmul(w4.w, vv[j])));
+                        }
+                    }
+                }
+            }
+            // the rest: each row up to its own position
+            for (; t <= p_last; t++) {
                 const float v = widen(vt[(size_t)t * hd + i]);
 #pragma unroll
-                for (int r = 0; r < PF_ATT_MAX_ROWS; r++)
-                    if (t <= pr[r]) o[r] = fadd(o[r], fmul(pf_att[(size_t)r * a.p_cap + t], v));
+                for (int r = 0; r < RS; r++) {
+                    const int rr = r0 + r;
+                    if (r < rg && rr < rows && t <= a.start + b0 + rr / kv_mul) {
+                        const float w = pf_att[(size_t)t * rs + rr];
+                        if (r & 1) o[r >> 1].y = fadd(o[r >> 1].y, fmul(w, v));
+                        else o[r >> 1].x = fadd(o[r >> 1].x, fmul(w, v));
+                    }
+                }
             }
         }
-        // quantize per (token, head): 32 consecutive dimensions per warp
-        for (int r = 0; r < rows; r++) {
-            const int j = r / kv_mul, hm = r - j * kv_mul;
-            float orr = 0.0f;
+        // quantize per (token, head): a warp holds 32 consecutive dimensions of
+        // its group's rows
+        const bool warp_live = (groups > 1 ? (warp * 32) / hd < groups : i0 + warp * 32 < hd);
+        if (warp_live) {
 #pragma unroll
-            for (int rr = 0; rr < PF_ATT_MAX_ROWS; rr++)
-                if (rr == r) orr = o[rr];
-            if (i0 + warp * 32 < hd) {
-                float dq;
-                const int8_t q = quant_lane(orr, &dq);
-                const int gi = (kvh * kv_mul + hm) * hd + i;
-                a.xq[(size_t)(b0 + j) * a.k_pad + gi] = q;
-                if (lane == 0) a.xs[(size_t)(gi / 32) * a.n_pad + b0 + j] = dq;
+            for (int r = 0; r < RS; r++) {
+                const int rr = r0 + r;
+                if (r < rg && rr < rows) {
+                    const float orr = (r & 1) ? o[r >> 1].y : o[r >> 1].x;
+                    float dq;
+                    const int8_t q = quant_lane(orr, &dq);
+                    const int j = rr / kv_mul, hm = rr - j * kv_mul;
+                    const int gi = (kvh * kv_mul + hm) * hd + i;
+                    a.xq[(size_t)(b0 + j) * a.k_pad + gi] = q;
+                    if (lane == 0) a.xs[(size_t)(gi / 32) * a.n_pad + b0 + j] = dq;
+                }
             }
         }
     }

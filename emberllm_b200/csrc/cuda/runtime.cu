@@ -662,7 +662,7 @@ extern "C" int ember_cuda_prefill(EmberCudaState *s, const int *ids, int n, int 
     hc[CTL_POS] = start; hc[CTL_TOK] = 0; hc[CTL_NOUT] = 0; hc[CTL_BASE] = start; hc[CTL_ERR] = 0;
     CK(cudaMemcpyAsync(s->ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, s->stream));
     CK(cudaMemcpyAsync(s->ctl, hc, 5 * sizeof(int), cudaMemcpyHostToDevice, s->stream));
-    if (n > 1 && batched_prefill_enabled() && pf_supported(s->m)) {
+    if (n > 1 && batched_prefill_enabled() && pf_supported(s->m) && pf_fits(s, n, start)) {
         // all layers over the n tokens at once (tensor-core GEMMs), then the head
         if (pf_run_layers(s, s->ids, n, start)) return 1;
     } else {

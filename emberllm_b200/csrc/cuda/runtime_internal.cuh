@@ -108,6 +108,8 @@ int pf_supported(const EmberCudaModel *m);
 // filled for them; leaves the last token's residual stream in s->x. Enqueued on
 // s->stream.
 int pf_run_layers(EmberCudaState *s, const int *ids_dev, int n, int start);
+// 1 when a batched prefill of n tokens at `start` fits the attention tiling
+int pf_fits(EmberCudaState *s, int n, int start);
 void pf_model_release(EmberCudaModel *m);
 void pf_state_release(EmberCudaState *s);
 // op level: out[B][d_out] = W x for B host columns through the tensor-core GEMM;
