@@ -372,7 +372,10 @@ def run_ours(args, world, rank, local, dist):
     _, dk, dms, dbytes = kinds[0]
     peak, peak_kind = measured_peaks()
     achieved = dbytes / (dms / 1e3) / 1e9
-    launches = 1 + 5 * L + 1 + 1     # embed, 5 per layer, lm_head, argmax
+    # kernels of one greedy token: the forward graph's launches + argmax/advance
+    lib.ember_cuda_state_launches_per_step.restype = ctypes.c_int
+    lib.ember_cuda_state_launches_per_step.argtypes = [ctypes.c_void_p]
+    launches = lib.ember_cuda_state_launches_per_step(cs) + 1
     e.close()
 
     total_tokens = world * args.steps * ntok

@@ -162,6 +162,31 @@ EMB_DEV float chain_sum(float s, const float *v, int n) {
     return s;
 }
 
+// chain_sum for long arrays: the next 16 loads are in flight while the current
+// 16 values are added, so the chain runs at the adder's latency
+EMB_DEV float chain_sum_pipe(float s, const float *v, int n) {
+    if (n < 32) return chain_sum(s, v, n);
+    float a[16], b[16];
+#pragma unroll
+    for (int j = 0; j < 16; j++) a[j] = v[j];
+    int i = 16;
+    for (; i + 32 <= n; i += 32) {
+#pragma unroll
+        for (int j = 0; j < 16; j++) b[j] = v[i + j];
+#pragma unroll
+        for (int j = 0; j < 16; j++) s = __fadd_rn(s, a[j]);
+#pragma unroll
+        for (int j = 0; j < 16; j++) a[j] = v[i + 16 + j];
+#pragma unroll
+        for (int j = 0; j < 16; j++) s = __fadd_rn(s, b[j]);
+    }
+    // a holds v[i-16 .. i-1]
+#pragma unroll
+    for (int j = 0; j < 16; j++) s = __fadd_rn(s, a[j]);
+    for (; i < n; i++) s = __fadd_rn(s, v[i]);
+    return s;
+}
+
 // sum of v[i]*v[i] in index order (products rounded, then added)
 EMB_DEV float chain_sumsq(const float *v, int n) {
     float s = 0.0f;
@@ -201,6 +226,10 @@ EMB_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
         : "memory");
 }
 
+EMB_DEV void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 EMB_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -220,6 +249,18 @@ constexpr uint32_t MBAR_TRIES = 1u << 22;
 EMB_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
     for (uint32_t i = 0; i < MBAR_TRIES; i++)
         if (mbar_try_wait(bar, parity)) return true;
+    if (err) atomicExch(err, code);
+    return false;
+}
+
+// Bounded wait that backs off between polls (__nanosleep), for a thread whose
+// wait may be long while other warps of the CTA work out of shared memory:
+// a tight try_wait loop competes with their shared-memory accesses.
+EMB_DEV bool mbar_wait_backoff(uint64_t *bar, uint32_t parity, int *err, int code) {
+    for (uint32_t i = 0; i < MBAR_TRIES; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        __nanosleep(256);
+    }
     if (err) atomicExch(err, code);
     return false;
 }
@@ -257,6 +298,16 @@ struct ExpfDev {
     EmberExpfParams p;      // p.slots is a DEVICE pointer here
 };
 
-EMB_DEV float expf_exact(const ExpfDev &e, float x) { return exc_expf(&e.p, e.p.slots, x); }
+// With the 64-entry 2^(j/64) table copied to shared memory (tab_s, by
+// expf_table_load), so each call costs no global-memory latency; the exception
+// slots stay in global memory (rarely read).
+EMB_DEV float expf_exact(const ExpfDev &e, const double *tab_s, float x) {
+    return exc_expf_t(&e.p, tab_s, e.p.slots, x);
+}
+// threads 0..63 copy the table (static data: may run before the dependency wait);
+// the caller synchronises before the first expf_exact
+EMB_DEV void expf_table_load(double *tab_s, const ExpfDev &e) {
+    if (threadIdx.x < 64) tab_s[threadIdx.x] = e.p.tab[threadIdx.x];
+}
 
 }  // namespace emb

@@ -26,7 +26,6 @@
 #pragma once
 
 #include "common.cuh"
-#include "exact_sum.cuh"
 
 namespace emb {
 
@@ -88,7 +87,8 @@ __host__ __device__ inline size_t gemv_sub_bytes(int dtype, int rows, int cols) 
 // scratch instead
 __host__ __device__ inline size_t gemv_p_bytes(int cols, bool in_norm) {
     size_t p = (size_t)2 * GEMV_MAX_ROWS * gemv_p_stride(cols / 32) * 4;
-    size_t pro = in_norm ? (size_t)cols * 8 + sizeof(XsScratch) : (size_t)cols * 4;
+    size_t pro = (size_t)cols * 4;   // the prologue's norm weights (in_norm)
+    (void)in_norm;
     return pad16(p > pro ? p : pro);
 }
 
@@ -198,6 +198,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[GEMV_MAX_STAGES];
     __shared__ float s_scale;
+    __shared__ double tab_s[EPI == EPI_SWIGLU ? 64 : 1];
     constexpr int nsub = EPI == EPI_SWIGLU ? 2 : 1;
     const int tid = threadIdx.x, R = a.rows;
     const int cols = a.cols, nb = cols / 32, pstride = gemv_p_stride(nb);
@@ -229,12 +230,11 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
         for (int k = 0; k < S && k < my_tiles; k++)
             issue_tile<EPI>(a, blockIdx.x + k * gridDim.x, stage0 + (size_t)k * a.stage_bytes, &bars[k]);
     }
-    // until the tiles need P: the norm weights, the squares, the exact-sum scratch
+    // until the tiles need P: the norm weights
     float *nw_s = P;
-    float *sq_s = P + cols;
-    XsScratch *xs = reinterpret_cast<XsScratch *>(P + 2 * (size_t)cols);
     if (IN == IN_NORM)
         for (int i = tid; i < cols; i += GEMV_THREADS) nw_s[i] = a.norm_w[i];
+    if (EPI == EPI_SWIGLU) expf_table_load(tab_s, a.ex);
     EMB_PROBE(PK, 1);
     pdl_wait_then_release();
     EMB_PROBE(PK, 2);
@@ -256,8 +256,6 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
             if (tid == 0) s_scale = rms_scale(chain_sumsq(xf_s, cols), cols, a.eps);
             __syncthreads();
             EMB_PROBE(PK, 4);
-            (void)sq_s;
-            (void)xs;
             const float sc = s_scale;
             for (int i = tid; i < cols; i += GEMV_THREADS)
                 xf_s[i] = fmul(fmul(xf_s[i], sc), nw_s[i]);   // (x*scale)*w
@@ -361,7 +359,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
                 float h = 0.0f;
                 if (tid < nrows) {
                     float gv = rowsum[tid], uv = rowsum[GEMV_MAX_ROWS + tid];
-                    float e = expf_exact(a.ex, -gv);
+                    float e = expf_exact(a.ex, tab_s, -gv);
                     h = fmul(fdiv(gv, fadd(1.0f, e)), uv);
                     if (a.hf) a.hf[row0 + tid] = h;
                 }
@@ -456,7 +454,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
     __shared__ float2 cs_s[128];
     __shared__ float red[ATTN_THREADS / 32];
     __shared__ float s_q, s_k, s_max, s_inv;
-    __shared__ XsScratch xs;
+    __shared__ double tab_s[64];
     const int h = blockIdx.x, tid = threadIdx.x, hd = a.hd, CH = a.chunk;
     const int kv_mul = a.nh / a.nkv, kvh = h / kv_mul;
     const int warp = tid >> 5, lane = tid & 31;
@@ -483,6 +481,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
         kn_s[tid] = a.k_norm ? a.k_norm[tid] : 0.0f;
     }
     if (tid < hd / 2) cs_s[tid] = a.rope[(size_t)pos * (hd / 2) + tid];
+    expf_table_load(tab_s, a.ex);
     __syncthreads();
     const int nchunks = (pos + CH - 1) / CH;
     const int n0 = min(CH, pos);
@@ -596,16 +595,10 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
     }
     __syncthreads();
     const float mx = s_max;
-    for (int t = tid; t <= pos; t += ATTN_THREADS) att[t] = expf_exact(a.ex, fsub(att[t], mx));
+    for (int t = tid; t <= pos; t += ATTN_THREADS) att[t] = expf_exact(a.ex, tab_s, fsub(att[t], mx));
     __syncthreads();
-    // the denominator: the reference's sequential sum over t = 0..pos; long
-    // sums use the CTA-parallel exact evaluation
-    if (pos + 1 > 2048) {
-        const float den = exact_pos_sum<ATTN_THREADS>(att, pos + 1, &xs);
-        if (tid == 0) s_inv = fdiv(1.0f, den);
-    } else if (tid == 0) {
-        s_inv = fdiv(1.0f, chain_sum(0.0f, att, pos + 1));
-    }
+    // the denominator: the reference's sequential sum over t = 0..pos
+    if (tid == 0) s_inv = fdiv(1.0f, chain_sum(0.0f, att, pos + 1));
     __syncthreads();
     const float inv = s_inv;
     for (int t = tid; t <= pos; t += ATTN_THREADS) att[t] = fmul(att[t], inv);

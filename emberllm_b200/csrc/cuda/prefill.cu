@@ -70,6 +70,25 @@ static int map_i8(CUtensorMap *map, const void *base, size_t inner, size_t outer
     return 0;
 }
 
+// a 2-D fp32 / fp16 matrix [outer][inner] (row stride = inner elements), boxes
+// of box_inner x box_outer elements, no swizzle
+int map_2d(CUtensorMap *map, const void *base, int elem_bytes, size_t inner, size_t outer, int box_inner,
+           int box_outer) {
+    auto fn = encode_fn();
+    if (!fn) return set_err("cuTensorMapEncodeTiled is not available from the driver");
+    if ((inner * elem_bytes) % 16 || (box_inner * elem_bytes) % 16 || (uintptr_t)base % 16)
+        return set_err("tensor map: unaligned matrix");
+    cuuint64_t dims[2] = { (cuuint64_t)inner, (cuuint64_t)outer };
+    cuuint64_t strides[1] = { (cuuint64_t)inner * elem_bytes };
+    cuuint32_t box[2] = { (cuuint32_t)box_inner, (cuuint32_t)box_outer };
+    cuuint32_t es[2] = { 1u, 1u };
+    CUresult r = fn(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                    const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_err("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return 0;
+}
+
 // ------------------------------------------------------------ kernel setup ---
 
 template <typename K>

@@ -42,9 +42,6 @@ EMB_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
-EMB_DEV void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
 EMB_DEV unsigned long long global_ns() {
     unsigned long long t;
@@ -541,11 +538,14 @@ __global__ void __launch_bounds__(256) pf_norm_quant_kernel(const PfTokArgs a) {
 // h = g / (1 + expf(-g)) * u (ref src/model.c:403-406), then quantize.
 __global__ void __launch_bounds__(256) pf_swiglu_quant_kernel(const PfTokArgs a) {
     extern __shared__ __align__(16) float pf_row[];
+    __shared__ double tab_s[64];
     const int t = blockIdx.x;
+    expf_table_load(tab_s, a.ex);
+    __syncthreads();
     const float *xr = a.x + (size_t)t * a.ld_x;
     for (int i = threadIdx.x; i < a.cols; i += blockDim.x) {
         const float g = xr[i], u = xr[a.hidden + i];
-        pf_row[i] = fmul(fdiv(g, fadd(1.0f, expf_exact(a.ex, -g))), u);
+        pf_row[i] = fmul(fdiv(g, fadd(1.0f, expf_exact(a.ex, tab_s, -g))), u);
     }
     __syncthreads();
     pf_quant_row(pf_row, a, t);
@@ -665,11 +665,8 @@ struct PfAttnArgs {
     ExpfDev ex;
 };
 
-// shared memory of one attention CTA: the weights [p_cap][rs] and, when a row
-// has more than 2048 positions, one contiguous row for the exact parallel sum
-__host__ __device__ inline size_t pf_attn_smem(int p_cap, int rs) {
-    return (size_t)p_cap * rs * 4 + (p_cap > 2048 ? (size_t)p_cap * 4 : 0);
-}
+// shared memory of one attention CTA: the weights [p_cap][rs]
+__host__ __device__ inline size_t pf_attn_smem(int p_cap, int rs) { return (size_t)p_cap * rs * 4; }
 
 // One CTA per (kv head, tile of tq consecutive tokens); its query rows are the
 // tile's tokens x the kv head's query heads (row r = token r / kv_mul, head
@@ -678,8 +675,8 @@ __host__ __device__ inline size_t pf_attn_smem(int p_cap, int rs) {
 //   scores   sc_t = sum_i q_i*k_t,i in index order, * (1/sqrt(hd)) -- one thread
 //            per position, the 16 rows' chains side by side (each key element
 //            loaded once serves every row);
-//   softmax  max, e_t = expf(sc_t - max), den = sequential sum over t (CTA-
-//            parallel exact evaluation above 2048 terms), w_t = e_t * (1/den);
+//   softmax  max, e_t = expf(sc_t - max), den = sequential sum over t,
+//            w_t = e_t * (1/den);
 //   output   o_i = sum_t w_t*v_t,i in position order -- one thread per
 //            (dimension, row group), then quantized per (token, head).
 // Weights sit in shared memory as [position][rs rows], so the output loop
@@ -692,7 +689,7 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
     __shared__ __align__(16) float q_s[256 * PF_ATT_MAX_ROWS];   // [hd][16]
     __shared__ float red[PF_ATT_MAX_ROWS][PF_ATT_THREADS / 32];
     __shared__ float s_max[PF_ATT_MAX_ROWS], s_inv[PF_ATT_MAX_ROWS];
-    __shared__ XsScratch xs;
+    __shared__ double tab_s[64];
     constexpr int RS = PF_ATT_MAX_ROWS;   // q_s stride and register rows
     const int rs = a.rs;                  // weight stride in shared memory (<= RS)
     const int kvh = blockIdx.x, b0 = blockIdx.y * a.tq, tid = threadIdx.x, hd = a.hd;
@@ -704,7 +701,7 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
     const int p_last = a.start + b0 + ntok - 1;      // the tile's last position
     const T *kt = reinterpret_cast<const T *>(a.kc) + (size_t)kvh * hd * a.kstride;
     const T *vt = reinterpret_cast<const T *>(a.vc) + (size_t)kvh * a.ctx * hd;
-    float *row_buf = pf_att + (size_t)a.p_cap * rs;  // contiguous row for long sums
+    expf_table_load(tab_s, a.ex);
     for (int idx = tid; idx < RS * hd; idx += PF_ATT_THREADS) {
         const int r = idx / hd, i = idx - r * hd;
         const int j = r / kv_mul, hm = r - j * kv_mul;
@@ -760,36 +757,23 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
     __syncthreads();
     for (int idx = tid; idx < (p_last + 1) * rs; idx += PF_ATT_THREADS) {
         const int t = idx / rs, r = idx - t * rs;
-        if (r < rows && t <= a.start + b0 + r / kv_mul) pf_att[idx] = expf_exact(a.ex, fsub(pf_att[idx], s_max[r]));
+        if (r < rows && t <= a.start + b0 + r / kv_mul) pf_att[idx] = expf_exact(a.ex, tab_s, fsub(pf_att[idx], s_max[r]));
     }
     __syncthreads();
-    // denominators: short sums as one chain per row (rows in parallel), long
-    // ones by the CTA-parallel exact evaluation over a contiguous copy
+    // denominators: the sequential sum over t, one chain per row (rows in parallel)
     if (tid < rows) {
         const int pr = a.start + b0 + tid / kv_mul;
-        if (pr + 1 <= 2048) {
-            float sum = 0.0f;
-            int t = 0;
-            for (; t + 8 <= pr + 1; t += 8) {
-                float e[8];
+        float sum = 0.0f;
+        int t = 0;
+        for (; t + 8 <= pr + 1; t += 8) {
+            float e[8];
 #pragma unroll
-                for (int j = 0; j < 8; j++) e[j] = pf_att[(size_t)(t + j) * rs + tid];
+            for (int j = 0; j < 8; j++) e[j] = pf_att[(size_t)(t + j) * rs + tid];
 #pragma unroll
-                for (int j = 0; j < 8; j++) sum = fadd(sum, e[j]);
-            }
-            for (; t <= pr; t++) sum = fadd(sum, pf_att[(size_t)t * rs + tid]);
-            s_inv[tid] = fdiv(1.0f, sum);
+            for (int j = 0; j < 8; j++) sum = fadd(sum, e[j]);
         }
-    }
-    for (int r = 0; r < rows; r++) {
-        const int pr = a.start + b0 + r / kv_mul;
-        if (pr + 1 > 2048) {
-            __syncthreads();
-            for (int t = tid; t <= pr; t += PF_ATT_THREADS) row_buf[t] = pf_att[(size_t)t * rs + r];
-            __syncthreads();
-            const float den = exact_pos_sum<PF_ATT_THREADS>(row_buf, pr + 1, &xs);
-            if (tid == 0) s_inv[r] = fdiv(1.0f, den);
-        }
+        for (; t <= pr; t++) sum = fadd(sum, pf_att[(size_t)t * rs + tid]);
+        s_inv[tid] = fdiv(1.0f, sum);
     }
     __syncthreads();
     for (int idx = tid; idx < (p_last + 1) * rs; idx += PF_ATT_THREADS) {

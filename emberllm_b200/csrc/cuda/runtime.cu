@@ -29,6 +29,7 @@
 #include "ember_cuda.h"
 #include "ember_ops.h"
 #include "kernels.cuh"
+#include "attn_split.cuh"
 #include "runtime_internal.cuh"
 
 using namespace emb;
@@ -90,7 +91,15 @@ static int init_kernel_attrs(int device) {
     CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
     if (allow_max_smem(gemv_kernel<IN_RAW, EPI_STORE>, optin) || allow_max_smem(gemv_kernel<IN_NORM, EPI_STORE>, optin) ||
         allow_max_smem(gemv_kernel<IN_NORM, EPI_SWIGLU>, optin) || allow_max_smem(gemv_kernel<IN_QUANT, EPI_RESID>, optin) ||
-        allow_max_smem(attn_decode_kernel<float>, optin) || allow_max_smem(attn_decode_kernel<__half>, optin))
+        allow_max_smem(attn_decode_kernel<float>, optin) || allow_max_smem(attn_decode_kernel<__half>, optin) ||
+        allow_max_smem(attn_scores_kernel<float, 1>, optin) || allow_max_smem(attn_scores_kernel<__half, 1>, optin) ||
+        allow_max_smem(attn_scores_kernel<float, 2>, optin) || allow_max_smem(attn_scores_kernel<__half, 2>, optin) ||
+        allow_max_smem(attn_scores_kernel<float, 4>, optin) || allow_max_smem(attn_scores_kernel<__half, 4>, optin) ||
+        allow_max_smem(attn_scores_kernel<float, 8>, optin) || allow_max_smem(attn_scores_kernel<__half, 8>, optin) ||
+        allow_max_smem(attn_softmax_pv_kernel<float, true>, optin) ||
+        allow_max_smem(attn_softmax_pv_kernel<__half, true>, optin) ||
+        allow_max_smem(attn_softmax_pv_kernel<float, false>, optin) ||
+        allow_max_smem(attn_softmax_pv_kernel<__half, false>, optin))
         return 1;
     if (device < 32) done_mask |= 1u << device;
     return 0;
@@ -255,7 +264,16 @@ extern "C" int ember_cuda_state_new(EmberCudaModel *m, int ctx, int kv_fp16, con
     rc |= salloc(s, (void **)&s->q, (size_t)qd * 4);
     rc |= salloc(s, (void **)&s->k, (size_t)kvd * 4);
     rc |= salloc(s, (void **)&s->v, (size_t)kvd * 4);
-    rc |= salloc(s, (void **)&s->att, s->att_in_smem ? 16 : (size_t)m->n_heads * ctx * 4);
+    // split attention (attn_split.cuh): AS_PER cached positions per scoring CTA;
+    // the softmax weights sit in shared memory when they fit
+    s->attn_split = m->n_heads / m->n_kv <= AS_MAX_KVMUL && hd <= 256 && hd % 32 == 0;
+    s->attn_splits = (ctx + AS_PER - 1) / AS_PER;
+    s->attn_w_smem = as_pv_smem(m->n_heads / m->n_kv, ctx, (int)es, 1) <= 200 * 1024;
+    s->att_stride = (ctx + 3) / 4 * 4;
+    rc |= salloc(s, (void **)&s->att, (size_t)m->n_heads * s->att_stride * 4 + 256);
+    if (s->attn_split && !s->attn_w_smem)
+        rc |= salloc(s, (void **)&s->wglob, (size_t)(hd / 32) * m->n_heads * s->att_stride * 4 + 256);
+    rc |= salloc(s, (void **)&s->pmax, (size_t)m->n_heads * s->attn_splits * 4);
     rc |= salloc(s, (void **)&s->oq, (size_t)qd + 16);
     rc |= salloc(s, (void **)&s->od, (size_t)qd / 32 * 4 + 16);
     rc |= salloc(s, (void **)&s->of, (size_t)qd * 4);
@@ -292,6 +310,21 @@ extern "C" int ember_cuda_state_new(EmberCudaModel *m, int ctx, int kv_fp16, con
         return 1;
     }
     memset(s->h_logits, 0, (size_t)m->vocab * 4);
+    if (s->attn_split) {
+        // per layer: the keys as one [n_kv*hd][kstride] matrix read in [hd][AS_PER]
+        // boxes, the values as one [n_kv*ctx][hd] matrix read in [AS_VB][32] boxes
+        s->kmaps.resize(m->n_layers);
+        s->vmaps.resize(m->n_layers);
+        for (int l = 0; l < m->n_layers; l++)
+            if (map_2d(&s->kmaps[l], (char *)s->kc + (size_t)l * s->k_layer_elems * es, (int)es,
+                       (size_t)s->kstride, (size_t)m->n_kv * hd, AS_PER, hd) ||
+                map_2d(&s->vmaps[l], (char *)s->vc + (size_t)l * s->v_layer_elems * es, (int)es, (size_t)hd,
+                       (size_t)m->n_kv * ctx, 32, AS_VB)) {
+                state_release(s);
+                delete s;
+                return 1;
+            }
+    }
     *out = s;
     return 0;
 }
@@ -327,14 +360,14 @@ static bool pdl_enabled() {
 }
 
 template <typename... KArgs, typename... Args>
-static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_t smem, cudaStream_t st,
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, int block, size_t smem, cudaStream_t st,
                               Args... args) {
     if (g_prof_events && g_prof_n < g_prof_cap) {
         cudaError_t e = cudaEventRecord(g_prof_events[g_prof_n++], st);
         if (e != cudaSuccess) return e;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)grid);
+    cfg.gridDim = grid;
     cfg.blockDim = dim3((unsigned)block);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -475,6 +508,41 @@ static int launch_layer(EmberCudaState *s, int kind, int l, int *count) {
             return 0;
         }
     case K_ATTN: {
+        if (s->attn_split) {
+            AttnSplitArgs as;
+            memset(&as, 0, sizeof(as));
+            as.q = s->q; as.k = s->k; as.v = s->v;
+            as.kc = (char *)s->kc + (size_t)l * s->k_layer_elems * es;
+            as.vc = (char *)s->vc + (size_t)l * s->v_layer_elems * es;
+            as.q_norm = L.q_norm; as.k_norm = L.k_norm;
+            as.rope = s->rope; as.ctl = s->ctl; as.att = s->att; as.pmax = s->pmax; as.wglob = s->wglob;
+            as.oq = s->oq; as.od = s->od; as.of = is_q(L.wo) ? nullptr : s->of;
+            as.nh = m->n_heads; as.nkv = m->n_kv; as.hd = hd; as.ctx = s->ctx; as.kstride = s->kstride;
+            as.neox = m->rope_neox; as.splits = s->attn_splits; as.w_smem = s->attn_w_smem;
+            as.ast = s->att_stride; as.eps = m->eps; as.ex = m->ex;
+            const dim3 g1((unsigned)m->n_kv, (unsigned)s->attn_splits), g2((unsigned)m->n_kv, (unsigned)(hd / 32));
+            const size_t sm1 = as_scores_smem(hd, (int)es);
+            const size_t sm2 = as_pv_smem(m->n_heads / m->n_kv, s->ctx, (int)es, s->attn_w_smem);
+            const int kv_mul = m->n_heads / m->n_kv;
+            const CUtensorMap &km = s->kmaps[l];
+            if (s->kv_fp16) {
+                if (kv_mul == 1) CK(launch_pdl(attn_scores_kernel<__half, 1>, g1, AS_THREADS, sm1, st, km, as));
+                else if (kv_mul == 2) CK(launch_pdl(attn_scores_kernel<__half, 2>, g1, AS_THREADS, sm1, st, km, as));
+                else if (kv_mul <= 4) CK(launch_pdl(attn_scores_kernel<__half, 4>, g1, AS_THREADS, sm1, st, km, as));
+                else CK(launch_pdl(attn_scores_kernel<__half, 8>, g1, AS_THREADS, sm1, st, km, as));
+                if (s->attn_w_smem) CK(launch_pdl(attn_softmax_pv_kernel<__half, true>, g2, AS_THREADS, sm2, st, s->vmaps[l], as));
+                else CK(launch_pdl(attn_softmax_pv_kernel<__half, false>, g2, AS_THREADS, sm2, st, s->vmaps[l], as));
+            } else {
+                if (kv_mul == 1) CK(launch_pdl(attn_scores_kernel<float, 1>, g1, AS_THREADS, sm1, st, km, as));
+                else if (kv_mul == 2) CK(launch_pdl(attn_scores_kernel<float, 2>, g1, AS_THREADS, sm1, st, km, as));
+                else if (kv_mul <= 4) CK(launch_pdl(attn_scores_kernel<float, 4>, g1, AS_THREADS, sm1, st, km, as));
+                else CK(launch_pdl(attn_scores_kernel<float, 8>, g1, AS_THREADS, sm1, st, km, as));
+                if (s->attn_w_smem) CK(launch_pdl(attn_softmax_pv_kernel<float, true>, g2, AS_THREADS, sm2, st, s->vmaps[l], as));
+                else CK(launch_pdl(attn_softmax_pv_kernel<float, false>, g2, AS_THREADS, sm2, st, s->vmaps[l], as));
+            }
+            (*count) += 2;
+            return 0;
+        }
         AttnArgs at;
         memset(&at, 0, sizeof(at));
         at.q = s->q; at.k = s->k; at.v = s->v;

@@ -3,6 +3,7 @@
 // Internal to the library: nothing here crosses the C ABI.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <vector>
@@ -84,6 +85,13 @@ struct EmberCudaState {
     int am_blocks = 0;
     int att_in_smem = 0, attn_chunk = 0;
     size_t attn_smem = 0;
+    int attn_split = 0, attn_splits = 1;   // split decode attention (attn_split.cuh)
+    int attn_w_smem = 0;                   // softmax weights held in shared memory
+    float *pmax = nullptr;
+    int att_stride = 0;                    // row stride of att (ctx rounded up to 4)
+    float *wglob = nullptr;                // softmax weights when they do not fit smem
+    std::vector<CUtensorMap> kmaps;        // per layer: keys as [n_kv*hd][kstride], [hd][AS_PER] boxes
+    std::vector<CUtensorMap> vmaps;        // per layer: values as [n_kv*ctx][hd], [AS_VB][32] boxes
     // pinned host
     float *h_logits = nullptr;
     int *h_ctl = nullptr;
@@ -112,6 +120,10 @@ int pf_run_layers(EmberCudaState *s, const int *ids_dev, int n, int start);
 int pf_fits(EmberCudaState *s, int n, int start);
 void pf_model_release(EmberCudaModel *m);
 void pf_state_release(EmberCudaState *s);
+// tensor map of a 2-D fp32 / fp16 matrix [outer][inner] read in boxes of
+// box_inner x box_outer elements (no swizzle)
+int map_2d(CUtensorMap *map, const void *base, int elem_bytes, size_t inner, size_t outer, int box_inner,
+           int box_outer);
 // op level: out[B][d_out] = W x for B host columns through the tensor-core GEMM;
 // xq_blocks (may be NULL) receives the columns' Q8_0 blocks
 int pf_matmul_batch(int device, float *out, const float *x, const DevMat &w, int B, void *xq_blocks);

@@ -45,8 +45,9 @@
 EXC_FN uint32_t exc_fbits(float f) { union { float f; uint32_t u; } c; c.f = f; return c.u; }
 EXC_FN float exc_bitsf(uint32_t u) { union { float f; uint32_t u; } c; c.u = u; return c.f; }
 
-/* exp(x) in double by the recipe above; x finite and within [p->lo, p->hi] */
-EXC_FN double exc_exp_double(const EmberExpfParams *p, float xf) {
+/* exp(x) in double by the recipe above with the 2^(j/64) table at `tab` (the
+ * device keeps a copy in shared memory); x finite and within [p->lo, p->hi] */
+EXC_FN double exc_exp_double_t(const EmberExpfParams *p, const double *tab, float xf) {
     double x = (double)xf;
     double t = EXC_ADD(EXC_MUL(x, p->inv_step), p->shifter);
     double kd = EXC_ADD(t, -p->shifter);
@@ -57,8 +58,10 @@ EXC_FN double exc_exp_double(const EmberExpfParams *p, float xf) {
     int j = k & 63, m = (k - j) / 64;
     union { unsigned long long u; double d; } s;
     s.u = (unsigned long long)((long long)m + 1023) << 52;
-    return EXC_MUL(EXC_MUL(q, p->tab[j]), s.d);
+    return EXC_MUL(EXC_MUL(q, tab[j]), s.d);
 }
+
+EXC_FN double exc_exp_double(const EmberExpfParams *p, float xf) { return exc_exp_double_t(p, p->tab, xf); }
 
 EXC_FN unsigned long long exc_dbits(double d) { union { double d; unsigned long long u; } c; c.d = d; return c.u; }
 
@@ -85,13 +88,13 @@ EXC_FN uint32_t exc_hash(uint32_t xb, uint32_t n_slots) {
     return (xb * 0x9E3779B1u) & (n_slots - 1u);
 }
 
-/* The full function: the C library's expf(x), given the host-built table. */
-EXC_FN float exc_expf(const EmberExpfParams *p, const uint32_t *slots, float x) {
+/* The full function: the C library's expf(x), given the host-built tables. */
+EXC_FN float exc_expf_t(const EmberExpfParams *p, const double *tab, const uint32_t *slots, float x) {
     if (x != x) return x + x;
     if (x < p->lo) return 0.0f;
     if (x > p->hi) return exc_bitsf(0x7F800000u);
     int flag = 0;
-    float r = exc_round(p, exc_exp_double(p, x), &flag);
+    float r = exc_round(p, exc_exp_double_t(p, tab, x), &flag);
     if (flag) {
         uint32_t xb = exc_fbits(x);
         uint32_t i = exc_hash(xb, p->n_slots);
@@ -104,6 +107,10 @@ EXC_FN float exc_expf(const EmberExpfParams *p, const uint32_t *slots, float x) 
         }
     }
     return r;
+}
+
+EXC_FN float exc_expf(const EmberExpfParams *p, const uint32_t *slots, float x) {
+    return exc_expf_t(p, p->tab, slots, x);
 }
 
 #endif /* EMBER_B200_EXPF_CORE_H */

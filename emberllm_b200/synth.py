@@ -58,6 +58,10 @@ CONFIGS = {
                          vocab_size=320, max_seq_len=256, rope_theta=100000.0, norm_eps=1e-5,
                          rope_style=ROPE_NEOX, tied=True, qk_norm=False, bias=False,
                          quant="q4_0"),
+    # eight query heads per kv head: the single-kernel decode attention path
+    "tiny-mqa": dict(dim=256, hidden_dim=384, n_layers=2, n_heads=8, n_kv_heads=1, head_dim=32,
+                     vocab_size=448, max_seq_len=256, rope_theta=10000.0, norm_eps=1e-5,
+                     rope_style=ROPE_NEOX, tied=True, qk_norm=True, bias=False, quant="q8_0"),
     # long contexts: batched prefill in several chunks and softmax sums past 2048 terms
     "tiny-long": dict(dim=128, hidden_dim=256, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=64,
                       vocab_size=512, max_seq_len=4096, rope_theta=1e6, norm_eps=1e-6,

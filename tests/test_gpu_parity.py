@@ -18,7 +18,7 @@ from . import helpers as H
 
 pytestmark = pytest.mark.gpu
 
-TINY = ["tiny-llama", "tiny-qwen3", "tiny-qwen2", "tiny-smol-q4", "tiny-f32"]
+TINY = ["tiny-llama", "tiny-qwen3", "tiny-qwen2", "tiny-smol-q4", "tiny-f32", "tiny-mqa"]
 REL_L2 = 1e-3
 
 

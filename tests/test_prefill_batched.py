@@ -62,7 +62,7 @@ def test_gemm_matches_reference_batch_matmul(prod, orc, dtype, shape):
     assert nd == 0, f"{nd} of {got.size} outputs differ"
 
 
-QUANT_TINY = ["tiny-llama", "tiny-qwen3", "tiny-qwen2", "tiny-smol-q4"]
+QUANT_TINY = ["tiny-llama", "tiny-qwen3", "tiny-qwen2", "tiny-smol-q4", "tiny-mqa"]
 
 
 @pytest.mark.parametrize("kv16", [0, 1])
@@ -122,5 +122,22 @@ def test_full_size_prefill(prod, orc, name, n):
         la, lb = a.forward(ta, pos), b.forward(tb, pos)
         assert_same(la, lb, f"{name} step {i}")
         pos += 1
+    a.close()
+    b.close()
+
+
+@pytest.mark.parametrize("kv16", [0, 1])
+def test_long_context_decode(prod, orc, kv16):
+    """decode past 3000 cached positions: the split attention's many position
+    splits and the exact parallel softmax denominator, bit-exact"""
+    path = synth.ensure_model("tiny-long")
+    rng = np.random.default_rng(9 + kv16)
+    a = prod.session(path, 4096, kv16)
+    b = orc.session(path, 4096, kv16)
+    ids = [int(t) for t in rng.integers(0, a.vocab, 3000)]
+    assert_same(a.prefill(ids), b.prefill(ids), "tiny-long prefill 3000")
+    for i in range(6):
+        t = int(rng.integers(0, a.vocab))
+        assert_same(a.forward(t, 3000 + i), b.forward(t, 3000 + i), f"tiny-long forward {3000 + i}")
     a.close()
     b.close()
