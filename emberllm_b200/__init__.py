@@ -75,3 +75,43 @@ class Ember:
 
     def __del__(self):
         self.close()
+
+
+class EmberBatch:
+    """Independent sequences decoded together on one model (the library's
+    ember_batch_* extension): per-stream prompts, then greedy steps of all
+    streams at once. Each stream's tokens equal its own single-sequence run."""
+
+    def __init__(self, ember, n_streams, ctx=0, kv_fp16=False, max_steps=256):
+        self.lib = ember.lib
+        self.vocab = ember.vocab
+        self.n = int(n_streams)
+        self.b = self.lib.ember_batch_new(ember.m, self.n, int(ctx), 1 if kv_fp16 else 0, int(max_steps))
+
+    def prefill(self, stream, ids):
+        """Prompt of one stream; returns the index of its greedy next token."""
+        arr = (ctypes.c_int * len(ids))(*[int(i) for i in ids])
+        p = self.lib.ember_batch_prefill(self.b, int(stream), arr, len(ids))
+        best, bv = 0, p[0]
+        for i in range(1, self.vocab):
+            if p[i] > bv:
+                best, bv = i, p[i]
+        return best
+
+    def greedy(self, toks, pos, n_steps, logits=False):
+        """n_steps greedy steps of every stream; returns tokens [n_steps][n] (and
+        the last step's logits [n][vocab] when asked)."""
+        t = (ctypes.c_int * self.n)(*[int(x) for x in toks])
+        p = (ctypes.c_int * self.n)(*[int(x) for x in pos])
+        out = (ctypes.c_int * (n_steps * self.n))()
+        lg = (ctypes.c_float * (self.n * self.vocab))() if logits else None
+        self.lib.ember_batch_greedy(self.b, t, p, int(n_steps), out,
+                                    ctypes.cast(lg, ctypes.POINTER(ctypes.c_float)) if logits else None)
+        toks_out = [[out[s * self.n + i] for i in range(self.n)] for s in range(n_steps)]
+        return (toks_out, lg) if logits else toks_out
+
+    def close(self):
+        if getattr(self, "b", None):
+            self.lib.ember_batch_free(self.b)
+            self.b = None
+

@@ -64,6 +64,9 @@ CUDA_SYMBOLS = [
     "ember_cuda_time_kernel", "ember_cuda_argmax_static", "ember_host_expf_params",
     "ember_host_expf_emulated",
     "ember_host_rope_table", "ember_forward_greedy", "ember_state_cuda",
+    "ember_cuda_batch_new", "ember_cuda_batch_free", "ember_cuda_batch_prefill", "ember_cuda_batch_greedy",
+    "ember_cuda_batch_stream", "ember_batch_new", "ember_batch_free", "ember_batch_prefill",
+    "ember_batch_greedy",
 ]
 
 _lib = None
@@ -115,6 +118,14 @@ def load(path=None):
     lib.ember_forward_greedy.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _IP]
     lib.ember_state_cuda.restype = _P
     lib.ember_state_cuda.argtypes = [_P]
+    lib.ember_batch_new.restype = _P
+    lib.ember_batch_new.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    lib.ember_batch_free.argtypes = [_P]
+    lib.ember_batch_prefill.restype = _FP
+    lib.ember_batch_prefill.argtypes = [_P, ctypes.c_int, _IP, ctypes.c_int]
+    lib.ember_batch_greedy.argtypes = [_P, _IP, _IP, ctypes.c_int, _IP, _FP]
+    lib.ember_cuda_batch_stream.restype = _P
+    lib.ember_cuda_batch_stream.argtypes = [_P]
     lib.ember_cuda_state_stream.restype = _P
     lib.ember_cuda_state_stream.argtypes = [_P]
     lib.ember_cuda_state_logits_dev.restype = _P

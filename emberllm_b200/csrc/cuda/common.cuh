@@ -187,16 +187,29 @@ EMB_DEV float chain_sum_pipe(float s, const float *v, int n) {
     return s;
 }
 
-// sum of v[i]*v[i] in index order (products rounded, then added)
+// sum of v[i]*v[i] in index order (products rounded, then added); the squares
+// of the next 16 elements are formed while the current 16 are added
 EMB_DEV float chain_sumsq(const float *v, int n) {
     float s = 0.0f;
     int i = 0;
-    for (; i + 16 <= n; i += 16) {
-        float r[16];
+    if (n >= 32) {
+        float a[16], b[16];
 #pragma unroll
-        for (int j = 0; j < 16; j++) r[j] = v[i + j];
+        for (int j = 0; j < 16; j++) a[j] = __fmul_rn(v[j], v[j]);
+        i = 16;
+        for (; i + 32 <= n; i += 32) {
 #pragma unroll
-        for (int j = 0; j < 16; j++) s = __fadd_rn(s, __fmul_rn(r[j], r[j]));
+            for (int j = 0; j < 16; j++) b[j] = __fmul_rn(v[i + j], v[i + j]);
+#pragma unroll
+            for (int j = 0; j < 16; j++) s = __fadd_rn(s, a[j]);
+#pragma unroll
+            for (int j = 0; j < 16; j++) a[j] = __fmul_rn(v[i + 16 + j], v[i + 16 + j]);
+#pragma unroll
+            for (int j = 0; j < 16; j++) s = __fadd_rn(s, b[j]);
+        }
+        // a holds the squares of v[i-16 .. i-1]
+#pragma unroll
+        for (int j = 0; j < 16; j++) s = __fadd_rn(s, a[j]);
     }
     for (; i < n; i++) s = __fadd_rn(s, __fmul_rn(v[i], v[i]));
     return s;

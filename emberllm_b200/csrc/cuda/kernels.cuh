@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
                 const int sub = tid / R, r = tid - sub * R;
                 if (r < tr[sub].nrows) {
                     const float *pr = P + ((size_t)sub * GEMV_MAX_ROWS + r) * pstride;
-                    rowsum[sub * GEMV_MAX_ROWS + r] = chain_sum(0.0f, pr, nb);
+                    rowsum[sub * GEMV_MAX_ROWS + r] = chain_sum_pipe(0.0f, pr, nb);
                 }
             }
         } else {

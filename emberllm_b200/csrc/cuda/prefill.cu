@@ -139,6 +139,8 @@ struct PfLayerPack {
 
 struct PfModel {
     std::vector<PfLayerPack> layers;
+    PfMat head;                // lm_head, for batched decode (built on first use)
+    int head_ready = 0;
     std::vector<void *> allocs;
 };
 
@@ -239,13 +241,12 @@ struct PfState {
     std::vector<void *> allocs;
 };
 
-static int pf_prepare_state(EmberCudaState *s) {
-    if (s->pf) return 0;
-    EmberCudaModel *m = s->m;
+// activations for up to n_cap token rows
+static int pf_state_new(EmberCudaModel *m, int n_cap, PfState **out) {
     PfState *ps = new PfState();
     const int hd = m->head_dim, qd = m->n_heads * hd, kvd = m->n_kv * hd;
-    ps->n_cap = PF_CHUNK;
-    ps->n_pad = (int)round_up(PF_CHUNK, 128);
+    ps->n_cap = n_cap;
+    ps->n_pad = (int)round_up((size_t)n_cap, 128);
     const int ks[3] = { m->dim, qd, m->hidden };
     size_t kmax = 0;
     int nbmax = 0;
@@ -275,8 +276,19 @@ static int pf_prepare_state(EmberCudaState *s) {
         delete ps;
         return 1;
     }
-    s->pf = ps;
+    *out = ps;
     return 0;
+}
+
+static void pf_state_free(PfState *ps) {
+    if (!ps) return;
+    for (void *p : ps->allocs) cudaFree(p);
+    delete ps;
+}
+
+static int pf_prepare_state(EmberCudaState *s) {
+    if (s->pf) return 0;
+    return pf_state_new(s->m, PF_CHUNK, &s->pf);
 }
 
 void pf_state_release(EmberCudaState *s) {
@@ -353,82 +365,104 @@ int pf_fits(EmberCudaState *s, int n, int start) {
     return attn_tile(s->m, (int)round_up((size_t)(start + n), 4), &tq, &rs);
 }
 
+// The rows' positions and where their keys and values go: consecutive
+// positions start.. in one cache (prefill), or each row its own position pos[t]
+// and its own cache at kc/vc + t * cache_stride (batched decode of streams).
+struct PfSeq {
+    int n, start;
+    const int *pos;
+    size_t cache_stride;             // elements
+    void *kc, *vc;                   // layer-0 cache of row 0
+    size_t k_layer, v_layer;         // elements per layer
+    int ctx, kstride, kv_fp16;
+    const float2 *rope;
+    int tq, rs, p_cap;               // attention tiling
+};
+
+// embedding + every layer for q.n token rows of ids_dev, on ps->X
+static int pf_layers(EmberCudaModel *m, PfState *ps, const PfSeq &q, const int *ids_dev, int *err, cudaStream_t st) {
+    const int nc = q.n, hd = m->head_dim;
+    const size_t es = q.kv_fp16 ? 2 : 4;
+    {
+        PfEmbedArgs ea;
+        ea.q = m->tok_emb.q; ea.s = m->tok_emb.s; ea.dtype = m->tok_emb.dtype; ea.dim = m->dim;
+        ea.vocab = m->vocab; ea.ids = ids_dev; ea.x = ps->X; ea.err = err;
+        pf_embed_kernel<<<nc, 256, 0, st>>>(ea);
+        CK(cudaGetLastError());
+    }
+    for (int l = 0; l < m->n_layers; l++) {
+        const DevLayer &L = m->layers[l];
+        const PfLayerPack &P = m->pf->layers[l];
+        PfTokArgs ta;
+        memset(&ta, 0, sizeof(ta));
+        ta.xq = ps->XQ; ta.xs = ps->XS; ta.n_pad = ps->n_pad; ta.ex = m->ex; ta.eps = m->eps;
+        // attention block
+        ta.x = ps->X; ta.ld_x = m->dim; ta.norm_w = L.attn_norm; ta.cols = m->dim; ta.k_pad = ps->k_pad[PF_K_DIM];
+        pf_norm_quant_kernel<<<nc, 256, (size_t)m->dim * 4, st>>>(ta);
+        CK(cudaGetLastError());
+        if (launch_gemm(P.qkv, ps->mapB[PF_K_DIM], ps->XS, ps->n_pad, nc, ps->QKV, ps->ld_qkv, false, err, m->n_sm, st))
+            return 1;
+        PfQkvArgs qa;
+        qa.qkv = ps->QKV; qa.ld = ps->ld_qkv; qa.bq = L.bq; qa.bk = L.bk; qa.bv = L.bv;
+        qa.q_norm = m->qk_norm ? L.q_norm : nullptr; qa.k_norm = m->qk_norm ? L.k_norm : nullptr;
+        qa.rope = q.rope; qa.qr = ps->QR;
+        qa.kc = (char *)q.kc + (size_t)l * q.k_layer * es;
+        qa.vc = (char *)q.vc + (size_t)l * q.v_layer * es;
+        qa.nh = m->n_heads; qa.nkv = m->n_kv; qa.hd = hd; qa.ctx = q.ctx; qa.kstride = q.kstride;
+        qa.neox = m->rope_neox; qa.start = q.start; qa.pos = q.pos; qa.cache_stride = q.cache_stride; qa.eps = m->eps;
+        const dim3 qgrid((unsigned)nc, (unsigned)(m->n_heads + m->n_kv));
+        if (q.kv_fp16) pf_qkv_post_kernel<__half><<<qgrid, 256, 0, st>>>(qa);
+        else pf_qkv_post_kernel<float><<<qgrid, 256, 0, st>>>(qa);
+        CK(cudaGetLastError());
+        PfAttnArgs aa;
+        aa.qr = ps->QR; aa.kc = qa.kc; aa.vc = qa.vc; aa.xq = ps->XQ; aa.k_pad = ps->k_pad[PF_K_QD];
+        aa.xs = ps->XS; aa.n_pad = ps->n_pad; aa.nh = m->n_heads; aa.nkv = m->n_kv; aa.hd = hd;
+        aa.ctx = q.ctx; aa.kstride = q.kstride; aa.start = q.start; aa.n = nc; aa.tq = q.tq; aa.rs = q.rs;
+        aa.p_cap = q.p_cap; aa.pos = q.pos; aa.cache_stride = q.cache_stride; aa.ex = m->ex;
+        const dim3 agrid((unsigned)m->n_kv, (unsigned)((nc + q.tq - 1) / q.tq));
+        const size_t asmem = pf_attn_smem(q.p_cap, q.rs);
+        if (q.kv_fp16) pf_attn_kernel<__half><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
+        else pf_attn_kernel<float><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
+        CK(cudaGetLastError());
+        if (launch_gemm(P.wo, ps->mapB[PF_K_QD], ps->XS, ps->n_pad, nc, ps->X, m->dim, true, err, m->n_sm, st))
+            return 1;
+        // feed-forward block
+        ta.x = ps->X; ta.ld_x = m->dim; ta.norm_w = L.ffn_norm; ta.cols = m->dim; ta.k_pad = ps->k_pad[PF_K_DIM];
+        pf_norm_quant_kernel<<<nc, 256, (size_t)m->dim * 4, st>>>(ta);
+        CK(cudaGetLastError());
+        if (launch_gemm(P.w13, ps->mapB[PF_K_DIM], ps->XS, ps->n_pad, nc, ps->H, ps->ld_h, false, err, m->n_sm, st))
+            return 1;
+        ta.x = ps->H; ta.ld_x = ps->ld_h; ta.norm_w = nullptr; ta.cols = m->hidden; ta.hidden = m->hidden;
+        ta.k_pad = ps->k_pad[PF_K_HID];
+        pf_swiglu_quant_kernel<<<nc, 256, (size_t)m->hidden * 4, st>>>(ta);
+        CK(cudaGetLastError());
+        if (launch_gemm(P.w2, ps->mapB[PF_K_HID], ps->XS, ps->n_pad, nc, ps->X, m->dim, true, err, m->n_sm, st))
+            return 1;
+    }
+    return 0;
+}
+
 int pf_run_layers(EmberCudaState *s, const int *ids_dev, int n, int start) {
     EmberCudaModel *m = s->m;
     if (pf_prepare_model(m) || pf_prepare_state(s)) return 1;
     PfState *ps = s->pf;
-    cudaStream_t st = s->stream;
-    int *err = s->ctl + CTL_ERR;
-    const int hd = m->head_dim, qd = m->n_heads * hd;
-    const size_t es = s->kv_fp16 ? 2 : 4;
-    int tq = 0, rs = 0;
-    const int p_cap = (int)round_up((size_t)(start + n), 4);
-    if (!attn_tile(m, p_cap, &tq, &rs)) return set_err("prefill: %d positions do not fit the attention tile", start + n);
+    PfSeq q;
+    memset(&q, 0, sizeof(q));
+    q.kc = s->kc; q.vc = s->vc; q.k_layer = s->k_layer_elems; q.v_layer = s->v_layer_elems;
+    q.ctx = s->ctx; q.kstride = s->kstride; q.kv_fp16 = s->kv_fp16; q.rope = s->rope;
+    q.p_cap = (int)round_up((size_t)(start + n), 4);
+    if (!attn_tile(m, q.p_cap, &q.tq, &q.rs))
+        return set_err("prefill: %d positions do not fit the attention tile", start + n);
     int nc = 0;
     for (int c0 = 0; c0 < n; c0 += ps->n_cap) {
         nc = n - c0 < ps->n_cap ? n - c0 : ps->n_cap;
-        const int st0 = start + c0;
-        {
-            PfEmbedArgs ea;
-            ea.q = m->tok_emb.q; ea.s = m->tok_emb.s; ea.dtype = m->tok_emb.dtype; ea.dim = m->dim;
-            ea.vocab = m->vocab; ea.ids = ids_dev + c0; ea.x = ps->X; ea.err = err;
-            pf_embed_kernel<<<nc, 256, 0, st>>>(ea);
-            CK(cudaGetLastError());
-        }
-        for (int l = 0; l < m->n_layers; l++) {
-            const DevLayer &L = m->layers[l];
-            const PfLayerPack &P = m->pf->layers[l];
-            PfTokArgs ta;
-            memset(&ta, 0, sizeof(ta));
-            ta.xq = ps->XQ; ta.xs = ps->XS; ta.n_pad = ps->n_pad; ta.ex = m->ex; ta.eps = m->eps;
-            // attention block
-            ta.x = ps->X; ta.ld_x = m->dim; ta.norm_w = L.attn_norm; ta.cols = m->dim; ta.k_pad = ps->k_pad[PF_K_DIM];
-            pf_norm_quant_kernel<<<nc, 256, (size_t)m->dim * 4, st>>>(ta);
-            CK(cudaGetLastError());
-            if (launch_gemm(P.qkv, ps->mapB[PF_K_DIM], ps->XS, ps->n_pad, nc, ps->QKV, ps->ld_qkv, false, err,
-                            m->n_sm, st))
-                return 1;
-            PfQkvArgs qa;
-            qa.qkv = ps->QKV; qa.ld = ps->ld_qkv; qa.bq = L.bq; qa.bk = L.bk; qa.bv = L.bv;
-            qa.q_norm = m->qk_norm ? L.q_norm : nullptr; qa.k_norm = m->qk_norm ? L.k_norm : nullptr;
-            qa.rope = s->rope; qa.qr = ps->QR;
-            qa.kc = (char *)s->kc + (size_t)l * s->k_layer_elems * es;
-            qa.vc = (char *)s->vc + (size_t)l * s->v_layer_elems * es;
-            qa.nh = m->n_heads; qa.nkv = m->n_kv; qa.hd = hd; qa.ctx = s->ctx; qa.kstride = s->kstride;
-            qa.neox = m->rope_neox; qa.start = st0; qa.eps = m->eps;
-            const dim3 qgrid((unsigned)nc, (unsigned)(m->n_heads + m->n_kv));
-            if (s->kv_fp16) pf_qkv_post_kernel<__half><<<qgrid, 256, 0, st>>>(qa);
-            else pf_qkv_post_kernel<float><<<qgrid, 256, 0, st>>>(qa);
-            CK(cudaGetLastError());
-            PfAttnArgs aa;
-            aa.qr = ps->QR; aa.kc = qa.kc; aa.vc = qa.vc; aa.xq = ps->XQ; aa.k_pad = ps->k_pad[PF_K_QD];
-            aa.xs = ps->XS; aa.n_pad = ps->n_pad; aa.nh = m->n_heads; aa.nkv = m->n_kv; aa.hd = hd;
-            aa.ctx = s->ctx; aa.kstride = s->kstride; aa.start = st0; aa.n = nc; aa.tq = tq; aa.rs = rs; aa.p_cap = p_cap;
-            aa.ex = m->ex;
-            const dim3 agrid((unsigned)m->n_kv, (unsigned)((nc + tq - 1) / tq));
-            const size_t asmem = pf_attn_smem(p_cap, rs);
-            if (s->kv_fp16) pf_attn_kernel<__half><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
-            else pf_attn_kernel<float><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
-            CK(cudaGetLastError());
-            if (launch_gemm(P.wo, ps->mapB[PF_K_QD], ps->XS, ps->n_pad, nc, ps->X, m->dim, true, err, m->n_sm, st))
-                return 1;
-            // feed-forward block
-            ta.x = ps->X; ta.ld_x = m->dim; ta.norm_w = L.ffn_norm; ta.cols = m->dim; ta.k_pad = ps->k_pad[PF_K_DIM];
-            pf_norm_quant_kernel<<<nc, 256, (size_t)m->dim * 4, st>>>(ta);
-            CK(cudaGetLastError());
-            if (launch_gemm(P.w13, ps->mapB[PF_K_DIM], ps->XS, ps->n_pad, nc, ps->H, ps->ld_h, false, err,
-                            m->n_sm, st))
-                return 1;
-            ta.x = ps->H; ta.ld_x = ps->ld_h; ta.norm_w = nullptr; ta.cols = m->hidden; ta.hidden = m->hidden;
-            ta.k_pad = ps->k_pad[PF_K_HID];
-            pf_swiglu_quant_kernel<<<nc, 256, (size_t)m->hidden * 4, st>>>(ta);
-            CK(cudaGetLastError());
-            if (launch_gemm(P.w2, ps->mapB[PF_K_HID], ps->XS, ps->n_pad, nc, ps->X, m->dim, true, err, m->n_sm, st))
-                return 1;
-        }
+        q.n = nc;
+        q.start = start + c0;
+        if (pf_layers(m, ps, q, ids_dev + c0, s->ctl + CTL_ERR, s->stream)) return 1;
     }
     // the last token's residual stream feeds the final norm + lm_head
-    CK(cudaMemcpyAsync(s->x, ps->X + (size_t)(nc - 1) * m->dim, (size_t)m->dim * 4, cudaMemcpyDeviceToDevice, st));
+    CK(cudaMemcpyAsync(s->x, ps->X + (size_t)(nc - 1) * m->dim, (size_t)m->dim * 4, cudaMemcpyDeviceToDevice,
+                       s->stream));
     return 0;
 }
 
@@ -502,6 +536,235 @@ int pf_matmul_batch(int device, float *out, const float *x, const DevMat &w, int
 }
 
 }  // namespace emb
+
+// ------------------------------------------------------------ streams --------
+// Batched greedy decode of independent streams (BASELINE's many-sequence
+// workload): every step runs all S streams' tokens through the layers as S
+// token rows -- the tensor-core GEMMs read each weight row once per token tile
+// -- with each row at its own position in its own KV cache, then the final norm,
+// the lm_head GEMM and a per-stream argmax. Per stream the arithmetic is the
+// single-token step's, so each stream's tokens equal its own greedy run.
+
+namespace emb {
+
+static int pf_prepare_head(EmberCudaModel *m) {
+    if (m->pf->head_ready) return 0;
+    if (m->lm_head.dtype == EMBER_DT_F32) return set_err("batched decode needs a quantized lm_head");
+    const DevMat *parts[1] = { &m->lm_head };
+    if (build_pack(m->pf, &m->pf->head, parts, 1)) return 1;
+    CK(cudaDeviceSynchronize());
+    m->pf->head_ready = 1;
+    return 0;
+}
+
+// first index of the strict maximum of each stream's logits (ref
+// src/sample.c:114-118); the stream's next token and position; out[step][S]
+__global__ void __launch_bounds__(256) batch_argmax_kernel(const float *logits, int ld, int vocab, int *tok,
+                                                          int *pos, int *out, const int *nout, int S) {
+    __shared__ float sv[256];
+    __shared__ int si[256];
+    const int s = blockIdx.x, tid = threadIdx.x;
+    const float *row = logits + (size_t)s * ld;
+    float bv = -INFINITY;
+    int bi = 0x7FFFFFFF;
+    for (int i = tid; i < vocab; i += 256) {
+        const float v = row[i];
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    }
+    sv[tid] = bv;
+    si[tid] = bi;
+    __syncthreads();
+    for (int st = 128; st > 0; st >>= 1) {
+        if (tid < st) {
+            const float v = sv[tid + st];
+            const int i = si[tid + st];
+            if (v > sv[tid] || (v == sv[tid] && i < si[tid])) { sv[tid] = v; si[tid] = i; }
+        }
+        __syncthreads();
+    }
+    if (tid == 0) {
+        const int idx = si[0] == 0x7FFFFFFF ? 0 : si[0];   // all NaN: the reference keeps index 0
+        tok[s] = idx;
+        pos[s] += 1;
+        out[(size_t)(*nout) * S + s] = idx;
+    }
+}
+
+__global__ void batch_advance_kernel(int *nout) {
+    if (threadIdx.x == 0) *nout += 1;
+}
+
+}  // namespace emb
+
+using namespace emb;
+
+struct EmberCudaBatch {
+    EmberCudaModel *m = nullptr;
+    int S = 0, ctx = 0, kv_fp16 = 0, max_steps = 0;
+    EmberCudaState *worker = nullptr;     // prompt prefill; its cache pointers are aimed at a stream
+    void *kc = nullptr, *vc = nullptr;    // [S][layers][...] in the worker's per-layer layout
+    size_t stride = 0;                    // elements per stream (keys' and values' caches alike)
+    int *tok = nullptr, *pos = nullptr, *out = nullptr, *nout = nullptr;
+    float *logits = nullptr;
+    int ld_log = 0;
+    PfState *ps = nullptr;
+    cudaGraphExec_t g_step = nullptr;
+    std::vector<void *> allocs;
+};
+
+static void batch_release(EmberCudaBatch *b) {
+    if (b->g_step) cudaGraphExecDestroy(b->g_step);
+    pf_state_free(b->ps);
+    for (void *p : b->allocs) cudaFree(p);
+    b->allocs.clear();
+    if (b->worker) ember_cuda_state_free(b->worker);
+}
+
+extern "C" int ember_cuda_batch_new(EmberCudaModel *m, int n_streams, int ctx, int kv_fp16, const float *rope_cs,
+                                    int max_steps, EmberCudaBatch **out) {
+    *out = nullptr;
+    CK(cudaSetDevice(m->device));
+    if (n_streams < 1 || n_streams > PF_CHUNK) return set_err("batch: n_streams must be in [1, %d]", PF_CHUNK);
+    if (max_steps < 1) return set_err("batch: max_steps must be positive");
+    if (!pf_supported(m)) return set_err("batch: the model's layer weights are not all Q8_0 / Q4_0");
+    EmberCudaBatch *b = new EmberCudaBatch();
+    b->m = m; b->S = n_streams; b->ctx = ctx; b->kv_fp16 = kv_fp16 ? 1 : 0; b->max_steps = max_steps;
+    int rc = ember_cuda_state_new(m, ctx, b->kv_fp16, rope_cs, &b->worker);
+    if (!rc) rc = pf_prepare_model(m) || pf_init(m->device) || pf_prepare_head(m);
+    const size_t es = b->kv_fp16 ? 2 : 4;
+    if (!rc) {
+        EmberCudaState *w = b->worker;
+        const size_t sk = (size_t)m->n_layers * w->k_layer_elems, sv = (size_t)m->n_layers * w->v_layer_elems;
+        b->stride = sk > sv ? sk : sv;
+        b->ld_log = m->pf->head.rows_pad;
+        rc = pf_alloc(b->allocs, &b->kc, b->stride * es * n_streams + 256) ||
+             pf_alloc(b->allocs, &b->vc, b->stride * es * n_streams + 256) ||
+             pf_alloc(b->allocs, (void **)&b->tok, (size_t)n_streams * 4) ||
+             pf_alloc(b->allocs, (void **)&b->pos, (size_t)n_streams * 4) ||
+             pf_alloc(b->allocs, (void **)&b->out, (size_t)max_steps * n_streams * 4) ||
+             pf_alloc(b->allocs, (void **)&b->nout, 16) ||
+             pf_alloc(b->allocs, (void **)&b->logits, (size_t)n_streams * b->ld_log * 4) ||
+             pf_state_new(m, n_streams, &b->ps);
+        if (!rc && (cudaMemset(b->kc, 0, b->stride * es * n_streams) != cudaSuccess ||
+                    cudaMemset(b->vc, 0, b->stride * es * n_streams) != cudaSuccess))
+            rc = set_err("batch: cache initialisation failed");
+    }
+    if (!rc) {
+        // attention of one row per stream: the whole context in the weight tile
+        int tq, rs;
+        if (!attn_tile(m, (int)round_up((size_t)ctx, 4), &tq, &rs))
+            rc = set_err("batch: a context of %d does not fit the attention tile", ctx);
+    }
+    if (rc) {
+        batch_release(b);
+        delete b;
+        return 1;
+    }
+    *out = b;
+    return 0;
+}
+
+extern "C" void ember_cuda_batch_free(EmberCudaBatch *b) {
+    if (!b) return;
+    cudaSetDevice(b->m->device);
+    cudaStreamSynchronize(b->worker ? b->worker->stream : nullptr);
+    batch_release(b);
+    delete b;
+}
+
+extern "C" void *ember_cuda_batch_stream(EmberCudaBatch *b) { return (void *)b->worker->stream; }
+
+// the worker state's cache pointers aimed at stream i's cache
+static void aim_worker(EmberCudaBatch *b, int i) {
+    const size_t es = b->kv_fp16 ? 2 : 4;
+    b->worker->kc = (char *)b->kc + (size_t)i * b->stride * es;
+    b->worker->vc = (char *)b->vc + (size_t)i * b->stride * es;
+}
+
+extern "C" int ember_cuda_batch_prefill(EmberCudaBatch *b, int stream, const int *ids, int n, float *host_logits) {
+    CK(cudaSetDevice(b->m->device));
+    if (stream < 0 || stream >= b->S) return set_err("batch: stream %d out of range", stream);
+    if (n < 1 || n > b->ctx) return set_err("batch: prompt of %d tokens does not fit the context", n);
+    EmberCudaState *w = b->worker;
+    aim_worker(b, stream);
+    // the batched prefill (also for one token: the decode graphs of the worker
+    // address its own cache, never a stream's)
+    return ember_cuda_prefill_batched(w, ids, n, 0, host_logits);
+}
+
+// one greedy step of every stream, recorded once into a graph
+static int batch_record(EmberCudaBatch *b) {
+    EmberCudaModel *m = b->m;
+    EmberCudaState *w = b->worker;
+    cudaStream_t st = w->stream;
+    int *err = w->ctl + CTL_ERR;
+    PfSeq q;
+    memset(&q, 0, sizeof(q));
+    q.n = b->S; q.start = 0; q.pos = b->pos;
+    q.kc = b->kc; q.vc = b->vc; q.cache_stride = b->stride;
+    q.k_layer = w->k_layer_elems; q.v_layer = w->v_layer_elems;
+    q.ctx = b->ctx; q.kstride = w->kstride; q.kv_fp16 = b->kv_fp16; q.rope = w->rope;
+    q.p_cap = (int)round_up((size_t)b->ctx, 4);
+    q.tq = 1;
+    q.rs = (m->n_heads / m->n_kv + 3) / 4 * 4;
+    if (pf_layers(m, b->ps, q, b->tok, err, st)) return 1;
+    // final norm + lm_head over the S rows, then each stream's argmax
+    PfState *ps = b->ps;
+    PfTokArgs ta;
+    memset(&ta, 0, sizeof(ta));
+    ta.xq = ps->XQ; ta.xs = ps->XS; ta.n_pad = ps->n_pad; ta.ex = m->ex; ta.eps = m->eps;
+    ta.x = ps->X; ta.ld_x = m->dim; ta.norm_w = m->final_norm; ta.cols = m->dim; ta.k_pad = ps->k_pad[PF_K_DIM];
+    pf_norm_quant_kernel<<<b->S, 256, (size_t)m->dim * 4, st>>>(ta);
+    CK(cudaGetLastError());
+    if (launch_gemm(m->pf->head, ps->mapB[PF_K_DIM], ps->XS, ps->n_pad, b->S, b->logits, b->ld_log, false, err,
+                    m->n_sm, st))
+        return 1;
+    batch_argmax_kernel<<<b->S, 256, 0, st>>>(b->logits, b->ld_log, m->vocab, b->tok, b->pos, b->out, b->nout, b->S);
+    CK(cudaGetLastError());
+    batch_advance_kernel<<<1, 32, 0, st>>>(b->nout);
+    CK(cudaGetLastError());
+    return 0;
+}
+
+extern "C" int ember_cuda_batch_greedy(EmberCudaBatch *b, const int *toks, const int *pos, int n_steps,
+                                       int *host_tokens, float *host_logits) {
+    CK(cudaSetDevice(b->m->device));
+    if (n_steps < 1 || n_steps > b->max_steps) return set_err("batch: n_steps must be in [1, %d]", b->max_steps);
+    for (int i = 0; i < b->S; i++) {
+        if (toks[i] < 0 || toks[i] >= b->m->vocab) return set_err("batch: token id %d out of range", toks[i]);
+        if (pos[i] < 0 || pos[i] + n_steps > b->ctx) return set_err("batch: stream %d does not fit the context", i);
+    }
+    cudaStream_t st = b->worker->stream;
+    if (!b->g_step) {
+        cudaGraph_t g = nullptr;
+        CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        int rc = batch_record(b);
+        cudaError_t e = cudaStreamEndCapture(st, &g);
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return 1;
+        }
+        if (e != cudaSuccess) return set_err("batch graph capture failed: %s", cudaGetErrorString(e));
+        e = cudaGraphInstantiate(&b->g_step, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return set_err("batch graph instantiate failed: %s", cudaGetErrorString(e));
+    }
+    CK(cudaMemcpyAsync(b->tok, toks, (size_t)b->S * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(b->pos, pos, (size_t)b->S * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemsetAsync(b->nout, 0, 4, st));
+    CK(cudaMemsetAsync(b->worker->ctl + CTL_ERR, 0, 4, st));
+    for (int i = 0; i < n_steps; i++) CK(cudaGraphLaunch(b->g_step, st));
+    if (host_tokens)
+        CK(cudaMemcpyAsync(host_tokens, b->out, (size_t)n_steps * b->S * 4, cudaMemcpyDeviceToHost, st));
+    if (host_logits)
+        CK(cudaMemcpy2DAsync(host_logits, (size_t)b->m->vocab * 4, b->logits, (size_t)b->ld_log * 4,
+                             (size_t)b->m->vocab * 4, (size_t)b->S, cudaMemcpyDeviceToHost, st));
+    int herr = 0;
+    CK(cudaMemcpyAsync(&herr, b->worker->ctl + CTL_ERR, 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (herr) return set_err("batch: device wait timed out (code %d)", herr);
+    return 0;
+}
 
 #ifdef EMBER_PROBES
 // profiling build only: the last GEMM launch's trace (1024 timestamps)

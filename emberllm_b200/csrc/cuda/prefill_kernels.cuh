@@ -22,7 +22,6 @@
 #include <cuda.h>
 
 #include "common.cuh"
-#include "exact_sum.cuh"
 
 namespace emb {
 
@@ -590,6 +589,8 @@ struct PfQkvArgs {
     float *qr;             // [n][qd] roped queries
     void *kc, *vc;         // this layer's cache: keys [n_kv][hd][kstride], values [n_kv][ctx][hd]
     int nh, nkv, hd, ctx, kstride, neox, start;
+    const int *pos;        // batched decode: token t's position pos[t] (device) and
+    size_t cache_stride;   //   its own cache at kc/vc + t * cache_stride elements
     float eps;
 };
 
@@ -601,7 +602,8 @@ __global__ void __launch_bounds__(256) pf_qkv_post_kernel(const PfQkvArgs a) {
     __shared__ float vals[256];
     __shared__ float s_scale;
     const int t = blockIdx.x, hh = blockIdx.y, tid = threadIdx.x, hd = a.hd;
-    const int pos = a.start + t;
+    const int pos = a.pos ? a.pos[t] : a.start + t;
+    const size_t coff = a.pos ? (size_t)t * a.cache_stride : 0;
     const int qd = a.nh * hd, kvd = a.nkv * hd;
     const bool is_q = hh < a.nh;
     const int head = is_q ? hh : hh - a.nh;
@@ -633,8 +635,8 @@ __global__ void __launch_bounds__(256) pf_qkv_post_kernel(const PfQkvArgs a) {
         if (is_q) {
             a.qr[(size_t)t * qd + head * hd + tid] = vals[tid];
         } else {
-            T *kt = reinterpret_cast<T *>(a.kc) + (size_t)head * hd * a.kstride;
-            T *vt = reinterpret_cast<T *>(a.vc) + (size_t)head * a.ctx * hd;
+            T *kt = reinterpret_cast<T *>(a.kc) + coff + (size_t)head * hd * a.kstride;
+            T *vt = reinterpret_cast<T *>(a.vc) + coff + (size_t)head * a.ctx * hd;
             T kq, vq;
             kv_round(vals[tid], &kq);
             float v = row[qd + kvd + head * hd + tid];
@@ -661,6 +663,8 @@ struct PfAttnArgs {
     int nh, nkv, hd, ctx, kstride, start, n;
     int tq;                // tokens per CTA; rows = tq * (nh / nkv) <= PF_ATT_MAX_ROWS
     int rs;                // weight row stride: rows rounded up to 4
+    const int *pos;        // batched decode (tq = 1): token t's position pos[t] and its
+    size_t cache_stride;   //   own cache at kc/vc + t * cache_stride elements
     int p_cap;             // positions held in shared memory (>= start + n)
     ExpfDev ex;
 };
@@ -697,10 +701,13 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
     const int ntok = min(a.tq, a.n - b0);
     const int rows = ntok * kv_mul;
     const int qd = a.nh * hd;
-    const int p_first = a.start + b0;                // every row sees positions 0..p_first
-    const int p_last = a.start + b0 + ntok - 1;      // the tile's last position
-    const T *kt = reinterpret_cast<const T *>(a.kc) + (size_t)kvh * hd * a.kstride;
-    const T *vt = reinterpret_cast<const T *>(a.vc) + (size_t)kvh * a.ctx * hd;
+    // position of the tile's first token (rows of token j sit at pos0 + j)
+    const int pos0 = a.pos ? a.pos[b0] : a.start + b0;
+    const size_t coff = a.pos ? (size_t)b0 * a.cache_stride : 0;
+    const int p_first = pos0;                        // every row sees positions 0..p_first
+    const int p_last = pos0 + ntok - 1;              // the tile's last position
+    const T *kt = reinterpret_cast<const T *>(a.kc) + coff + (size_t)kvh * hd * a.kstride;
+    const T *vt = reinterpret_cast<const T *>(a.vc) + coff + (size_t)kvh * a.ctx * hd;
     expf_table_load(tab_s, a.ex);
     for (int idx = tid; idx < RS * hd; idx += PF_ATT_THREADS) {
         const int r = idx / hd, i = idx - r * hd;
@@ -742,7 +749,7 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
     // ---- softmax ----
     const int warp = tid >> 5, lane = tid & 31;
     for (int r = 0; r < rows; r++) {
-        const int pr = a.start + b0 + r / kv_mul;   // this row's position
+        const int pr = pos0 + r / kv_mul;   // this row's position
         float m = -INFINITY;
         for (int t = tid; t <= pr; t += PF_ATT_THREADS) m = fmaxf(m, pf_att[(size_t)t * rs + r]);
         m = warp_max(m);
@@ -757,12 +764,12 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
     __syncthreads();
     for (int idx = tid; idx < (p_last + 1) * rs; idx += PF_ATT_THREADS) {
         const int t = idx / rs, r = idx - t * rs;
-        if (r < rows && t <= a.start + b0 + r / kv_mul) pf_att[idx] = expf_exact(a.ex, tab_s, fsub(pf_att[idx], s_max[r]));
+        if (r < rows && t <= pos0 + r / kv_mul) pf_att[idx] = expf_exact(a.ex, tab_s, fsub(pf_att[idx], s_max[r]));
     }
     __syncthreads();
     // denominators: the sequential sum over t, one chain per row (rows in parallel)
     if (tid < rows) {
-        const int pr = a.start + b0 + tid / kv_mul;
+        const int pr = pos0 + tid / kv_mul;
         float sum = 0.0f;
         int t = 0;
         for (; t + 8 <= pr + 1; t += 8) {
@@ -778,7 +785,7 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
     __syncthreads();
     for (int idx = tid; idx < (p_last + 1) * rs; idx += PF_ATT_THREADS) {
         const int t = idx / rs, r = idx - t * rs;
-        if (r < rows && t <= a.start + b0 + r / kv_mul) pf_att[idx] = fmul(pf_att[idx], s_inv[r]);
+        if (r < rows && t <= pos0 + r / kv_mul) pf_att[idx] = fmul(pf_att[idx], s_inv[r]);
     }
     __syncthreads();
 
@@ -818,7 +825,7 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
 #pragma unroll
                 for (int r = 0; r < RS; r++) {
                     const int rr = r0 + r;
-                    if (r < rg && rr < rows && t <= a.start + b0 + rr / kv_mul) {
+                    if (r < rg && rr < rows && t <= pos0 + rr / kv_mul) {
                         const float w = pf_att[(size_t)t * rs + rr];
                         if (r & 1) o[r >> 1].y = fadd(o[r >> 1].y, fmul(w, v));
                         else o[r >> 1].x = fadd(o[r >> 1].x, fmul(w, v));

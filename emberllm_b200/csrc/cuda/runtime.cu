@@ -721,16 +721,18 @@ static bool batched_prefill_enabled() {
     return v == 1;
 }
 
-extern "C" int ember_cuda_prefill(EmberCudaState *s, const int *ids, int n, int start, float *host_logits) {
+static int prefill_impl(EmberCudaState *s, const int *ids, int n, int start, float *host_logits, bool force_batched) {
     CK(cudaSetDevice(s->m->device));
     if (n <= 0) return 0;
+    if (force_batched && !(pf_supported(s->m) && pf_fits(s, n, start)))
+        return set_err("the batched prefill does not support this model or prompt length");
     if (!s->g_head && capture(s, &s->g_head, 3)) return 1;
     int *hc = s->h_ctl;
     CK(cudaStreamSynchronize(s->stream));
     hc[CTL_POS] = start; hc[CTL_TOK] = 0; hc[CTL_NOUT] = 0; hc[CTL_BASE] = start; hc[CTL_ERR] = 0;
     CK(cudaMemcpyAsync(s->ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, s->stream));
     CK(cudaMemcpyAsync(s->ctl, hc, 5 * sizeof(int), cudaMemcpyHostToDevice, s->stream));
-    if (n > 1 && batched_prefill_enabled() && pf_supported(s->m) && pf_fits(s, n, start)) {
+    if (force_batched || (n > 1 && batched_prefill_enabled() && pf_supported(s->m) && pf_fits(s, n, start))) {
         // all layers over the n tokens at once (tensor-core GEMMs), then the head
         if (pf_run_layers(s, s->ids, n, start)) return 1;
     } else {
@@ -742,6 +744,14 @@ extern "C" int ember_cuda_prefill(EmberCudaState *s, const int *ids, int n, int 
     if (read_error_word(s)) return 1;
     if (host_logits && host_logits != s->h_logits) memcpy(host_logits, s->h_logits, (size_t)s->m->vocab * 4);
     return 0;
+}
+
+extern "C" int ember_cuda_prefill(EmberCudaState *s, const int *ids, int n, int start, float *host_logits) {
+    return prefill_impl(s, ids, n, start, host_logits, false);
+}
+
+int ember_cuda_prefill_batched(EmberCudaState *s, const int *ids, int n, int start, float *host_logits) {
+    return prefill_impl(s, ids, n, start, host_logits, true);
 }
 
 extern "C" int ember_cuda_greedy(EmberCudaState *s, int tok, int pos, int n_steps, int *host_tokens,

@@ -107,6 +107,9 @@ static inline int salloc(EmberCudaState *s, void **p, size_t n) {
     return 0;
 }
 
+// ember_cuda_prefill that always takes the batched path (also for one token)
+int ember_cuda_prefill_batched(EmberCudaState *s, const int *ids, int n, int start, float *host_logits);
+
 // ---- batched prefill (prefill.cu) ----
 namespace emb {
 // 1 when every layer matrix is Q8_0 / Q4_0 and the shapes suit the tensor-core

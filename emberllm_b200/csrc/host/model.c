@@ -214,3 +214,58 @@ float *ember_forward_greedy(EmberModel *m, EmberState *s, int tok, int pos, int 
 }
 
 EmberCudaState *ember_state_cuda(EmberState *s) { return s->dev; }
+
+/* ---- batched greedy decode of independent streams (extension) ---- */
+struct EmberBatch {
+    EmberCudaBatch *dev;
+    int n_streams, ctx, vocab;
+    float *logits;            /* [vocab]: the last prompt's logits */
+};
+
+EmberBatch *ember_batch_new(EmberModel *m, int n_streams, int ctx_len, int kv_fp16, int max_steps) {
+    const EmberHeader *h = ember_model_header(m);
+    if (h->n_heads <= 0 || h->n_kv_heads <= 0 || h->n_heads % h->n_kv_heads != 0)
+        ember_die("n_heads (%d) must be a positive multiple of n_kv_heads (%d)", h->n_heads, h->n_kv_heads);
+    if (h->head_dim <= 0 || h->head_dim % EMBER_Q_BLOCK != 0 || h->head_dim > 256)
+        ember_die("head_dim %d is not supported (multiples of 32 up to 256)", h->head_dim);
+    ensure_uploaded(m);
+    EmberBatch *b = ember_xcalloc(1, sizeof(*b), "EmberBatch");
+    b->n_streams = n_streams;
+    b->vocab = h->vocab_size;
+    b->ctx = (ctx_len > 0 && ctx_len < h->max_seq_len) ? ctx_len : h->max_seq_len;
+    size_t n_rope = (size_t)b->ctx * (size_t)(h->head_dim / 2) * 2;
+    float *rope = ember_xmalloc(n_rope * sizeof(float), "rope table");
+    ember_host_rope_table(rope, b->ctx, h->head_dim, h->rope_theta);
+    cuda_check(ember_cuda_batch_new(m->dev, n_streams, b->ctx, kv_fp16 ? 1 : 0, rope, max_steps, &b->dev),
+               "batch");
+    free(rope);
+    b->logits = ember_xmalloc((size_t)b->vocab * sizeof(float), "batch logits");
+    return b;
+}
+
+void ember_batch_free(EmberBatch *b) {
+    if (!b) return;
+    ember_cuda_batch_free(b->dev);
+    free(b->logits);
+    free(b);
+}
+
+float *ember_batch_prefill(EmberBatch *b, int stream, const int *ids, int n) {
+    if (stream < 0 || stream >= b->n_streams) ember_die("stream %d out of range [0,%d)", stream, b->n_streams);
+    if (n <= 0 || n > b->ctx) ember_die("prompt of %d tokens does not fit the context of %d", n, b->ctx);
+    for (int i = 0; i < n; i++)
+        if (ids[i] < 0 || ids[i] >= b->vocab) ember_die("token id %d out of range [0,%d)", ids[i], b->vocab);
+    cuda_check(ember_cuda_batch_prefill(b->dev, stream, ids, n, b->logits), "batch prefill");
+    return b->logits;
+}
+
+void ember_batch_greedy(EmberBatch *b, const int *toks, const int *pos, int n_steps, int *out_tokens,
+                        float *out_logits) {
+    for (int i = 0; i < b->n_streams; i++) {
+        if (toks[i] < 0 || toks[i] >= b->vocab) ember_die("token id %d out of range [0,%d)", toks[i], b->vocab);
+        if (pos[i] < 0 || pos[i] + n_steps > b->ctx)
+            ember_die("stream %d: %d steps from position %d do not fit the context of %d", i, n_steps, pos[i],
+                      b->ctx);
+    }
+    cuda_check(ember_cuda_batch_greedy(b->dev, toks, pos, n_steps, out_tokens, out_logits), "batch greedy");
+}

@@ -129,6 +129,29 @@ int  ember_cuda_time_kernel(EmberCudaState *s, int kind, int reps, float *ms_per
  * calls that overlap on the GPU share the array and race. */
 int  ember_cuda_argmax_static(const float *logits, int n, int *out_index, void *stream);
 
+/* ---- batched greedy decode of independent streams ----
+ * No counterpart in the reference (which decodes one sequence per state); this
+ * is the many-sequence workload: n_streams independent sequences, each with its
+ * own KV cache of ctx positions, advanced together. Every step runs all streams'
+ * tokens through the layers as one batch (tensor-core GEMMs over the streams),
+ * each at its own position, then the final norm, lm_head and a per-stream greedy
+ * pick. Per stream the arithmetic is the single-sequence step's, so each
+ * stream's tokens and logits equal those of its own ember_forward run.
+ * Requires Q8_0/Q4_0 layer and lm_head weights; n_streams in [1, 512]. */
+typedef struct EmberCudaBatch EmberCudaBatch;
+int  ember_cuda_batch_new(EmberCudaModel *m, int n_streams, int ctx, int kv_fp16, const float *rope_cs,
+                          int max_steps, EmberCudaBatch **out);
+void ember_cuda_batch_free(EmberCudaBatch *b);
+/* prompt ids[0..n) of stream `stream` at positions 0..n-1 (batched prefill into
+ * the stream's cache); the last token's logits to host_logits (vocab floats) */
+int  ember_cuda_batch_prefill(EmberCudaBatch *b, int stream, const int *ids, int n, float *host_logits);
+/* n_steps greedy steps of every stream: stream i feeds toks[i] at pos[i], then
+ * its own greedy picks. host_tokens (may be NULL) gets [n_steps][n_streams]
+ * tokens; host_logits (may be NULL) the last step's logits [n_streams][vocab]. */
+int  ember_cuda_batch_greedy(EmberCudaBatch *b, const int *toks, const int *pos, int n_steps, int *host_tokens,
+                             float *host_logits);
+void *ember_cuda_batch_stream(EmberCudaBatch *b);                /* cudaStream_t */
+
 /* the state's pinned host logits buffer (vocab floats), owned by the state */
 float       *ember_cuda_state_host_logits(EmberCudaState *s);
 
@@ -159,6 +182,21 @@ float *ember_forward_greedy(EmberModel *m, EmberState *s, int tok, int pos, int 
                             int *out_tokens);
 /* the device-side state behind a public state (for timing hooks) */
 EmberCudaState *ember_state_cuda(EmberState *s);
+
+/* Batched greedy decode of n_streams independent sequences on one model (see
+ * ember_cuda_batch_*): prompts go in per stream, then every step advances all
+ * streams at once. Fatal errors follow the library's convention (ember_die). */
+typedef struct EmberBatch EmberBatch;
+EmberBatch *ember_batch_new(EmberModel *m, int n_streams, int ctx_len, int kv_fp16, int max_steps);
+void        ember_batch_free(EmberBatch *b);
+/* prompt of stream `stream` at positions 0..n-1; returns its last token's logits
+ * (vocab floats owned by the batch, valid until the next call) */
+float      *ember_batch_prefill(EmberBatch *b, int stream, const int *ids, int n);
+/* n_steps greedy steps: stream i feeds toks[i] at pos[i]; out_tokens (may be
+ * NULL) [n_steps][n_streams]; out_logits (may be NULL) [n_streams][vocab] of the
+ * last step */
+void        ember_batch_greedy(EmberBatch *b, const int *toks, const int *pos, int n_steps, int *out_tokens,
+                               float *out_logits);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -1,0 +1,84 @@
+"""GPU parity of the batched decode of independent streams (ember_batch_*).
+
+BASELINE's many-sequence workload runs 8 x N independent streams, each with its
+own prompt and greedy continuation. The library decodes them together (one
+tensor-core GEMM per weight matrix per step, each stream at its own position in
+its own cache); per stream the arithmetic is the single-sequence step's, so
+every stream must produce exactly the tokens of its own greedy run, and the last
+step's logits must equal the oracle's bit for bit.
+"""
+import numpy as np
+import pytest
+
+from emberllm_b200 import Ember, EmberBatch, synth
+
+from . import helpers as H
+from .test_gpu_parity import assert_same
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def orc():
+    H.ensure_built()
+    return H.Oracle()
+
+
+def oracle_stream(orc, path, prompt, n_steps, kv16, ctx):
+    """the oracle's greedy continuation of one stream: (first token, the next
+    n_steps tokens, the logits after the last fed token)"""
+    s = orc.session(path, ctx, kv16)
+    logits = s.prefill(prompt)
+    first = H.first_argmax(logits)
+    toks, t, pos = [], first, len(prompt)
+    for _ in range(n_steps):
+        logits = s.forward(t, pos)
+        t = H.first_argmax(logits)
+        toks.append(t)
+        pos += 1
+    s.close()
+    return first, toks, logits
+
+
+def run_batch(path, prompts, n_steps, kv16, ctx):
+    e = Ember(path)
+    b = EmberBatch(e, len(prompts), ctx=ctx, kv_fp16=kv16, max_steps=n_steps)
+    firsts = [b.prefill(i, p) for i, p in enumerate(prompts)]
+    toks, lg = b.greedy(firsts, [len(p) for p in prompts], n_steps, logits=True)
+    logits = np.ctypeslib.as_array(lg).reshape(len(prompts), e.vocab).copy()
+    b.close()
+    e.close()
+    return firsts, toks, logits
+
+
+@pytest.mark.parametrize("kv16", [0, 1])
+@pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen3", "tiny-qwen2", "tiny-smol-q4", "tiny-mqa"])
+def test_tiny_streams_match_single_sequence_runs(orc, name, kv16):
+    """five streams with prompts of 1..30 tokens, 12 steps together"""
+    path = synth.ensure_model(name)
+    vocab = H.header_of(path)["vocab_size"]
+    rng = np.random.default_rng(31 + kv16)
+    prompts = [[int(t) for t in rng.integers(0, vocab, n)] for n in (3, 9, 17, 1, 30)]
+    n_steps, ctx = 12, 64
+    firsts, toks, logits = run_batch(path, prompts, n_steps, kv16, ctx)
+    for i, p in enumerate(prompts):
+        f, want, want_logits = oracle_stream(orc, path, p, n_steps, kv16, ctx)
+        assert firsts[i] == f, f"{name} stream {i}: first token"
+        assert [toks[s][i] for s in range(n_steps)] == want, f"{name} stream {i}: greedy tokens"
+        assert_same(logits[i], want_logits, f"{name} stream {i} last logits")
+
+
+@pytest.mark.slow
+def test_qwen3_eight_streams(orc):
+    """the BASELINE streams architecture at full size: 8 streams (configs[4],
+    N = 1), 32-token prompts, 16 steps"""
+    path = synth.ensure_model("qwen3-0.6b")
+    rng = np.random.default_rng(4)
+    vocab = H.header_of(path)["vocab_size"]
+    prompts = [[int(t) for t in rng.integers(0, vocab, 32)] for _ in range(8)]
+    n_steps, ctx = 16, 64
+    firsts, toks, logits = run_batch(path, prompts, n_steps, 0, ctx)
+    for i, p in enumerate(prompts):
+        f, want, want_logits = oracle_stream(orc, path, p, n_steps, 0, ctx)
+        assert firsts[i] == f and [toks[s][i] for s in range(n_steps)] == want, f"stream {i}"
+        assert_same(logits[i], want_logits, f"qwen3 stream {i} last logits")
