@@ -266,7 +266,14 @@ extern "C" int ember_cuda_state_new(EmberCudaModel *m, int ctx, int kv_fp16, con
     rc |= salloc(s, (void **)&s->v, (size_t)kvd * 4);
     // split attention (attn_split.cuh): AS_PER cached positions per scoring CTA;
     // the softmax weights sit in shared memory when they fit
-    s->attn_split = m->n_heads / m->n_kv <= AS_MAX_KVMUL && hd <= 256 && hd % 32 == 0;
+    // Short contexts keep the single-kernel attention (one launch fewer per layer;
+    // measured faster up to a few hundred positions); longer ones split the cache
+    // over CTAs. EMBER_ATTN=fused / split forces one (for comparisons).
+    const char *attn_env = getenv("EMBER_ATTN");
+    const bool force_fused = attn_env && strcmp(attn_env, "fused") == 0;
+    const bool force_split = attn_env && strcmp(attn_env, "split") == 0;
+    s->attn_split = m->n_heads / m->n_kv <= AS_MAX_KVMUL && hd <= 256 && hd % 32 == 0 && !force_fused &&
+                    (force_split || ctx > 512);
     s->attn_splits = (ctx + AS_PER - 1) / AS_PER;
     s->attn_w_smem = as_pv_smem(m->n_heads / m->n_kv, ctx, (int)es, 1) <= 200 * 1024;
     s->att_stride = (ctx + 3) / 4 * 4;

@@ -47,10 +47,14 @@ def orc():
     return H.Oracle()
 
 
+@pytest.mark.parametrize("attn", ["fused", "split"])
 @pytest.mark.parametrize("kv16", [0, 1])
 @pytest.mark.parametrize("name", TINY)
-def test_tiny_teacher_forced_bitexact(prod, orc, name, kv16):
-    """prefill 24 random ids, then 40 forced forwards: every step's logits equal"""
+def test_tiny_teacher_forced_bitexact(prod, orc, name, kv16, attn, monkeypatch):
+    """prefill 24 random ids, then 40 forced forwards: every step's logits equal
+    (both decode attention paths: one kernel per head, and the cache split over
+    CTAs)"""
+    monkeypatch.setenv("EMBER_ATTN", attn)
     path = synth.ensure_model(name)
     a = prod.session(path, 0, kv16)
     b = orc.session(path, 0, kv16)
