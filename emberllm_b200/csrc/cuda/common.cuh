@@ -215,6 +215,109 @@ EMB_DEV float chain_sumsq(const float *v, int n) {
     return s;
 }
 
+// ---- a sequential sum of non-negative terms in a fraction of the chain's latency ----
+// sum = ((0 + v[0]) + v[1]) + ... + v[n-1] in index order, exactly as
+// chain_sum(0, v, n), computed by the block's NT threads over K segments of
+// m = n/K terms at once: one thread adds segment 0 from 0; for each later
+// segment k, NC threads add it from the NC consecutive floats centred on a
+// double estimate of the exact sum of the segments before it. The float sum of
+// i non-negative terms lies within (i-1)/2 ulps of the exact one and in practice
+// within a few (the roundings largely cancel). Walking the boundaries in order,
+// the chain that started from the float sum actually reached is the next sum.
+// When a boundary's sum falls outside its window (or is not finite) the rest is
+// added sequentially from there: the result is the loop's either way, only the
+// time differs. v: shared memory, 16-byte aligned; n a multiple of 16*K (else
+// one thread adds). The code stays small on purpose: it runs once per launch
+// from a cold instruction cache, where every extra instantiation costs time.
+template <int NT, int K = 4>
+EMB_DEV float split_chain_sum(const float *v, int n, int *hit = nullptr) {
+    constexpr int NC = 64, NB = K - 1;
+    static_assert(K >= 2 && NT >= NC * NB + 1 && NT % 32 == 0, "split_chain_sum: block too small");
+    __shared__ double red[NB][NT / 32];
+    __shared__ float cand[NB][NC];
+    __shared__ float first_part, answer;
+    const unsigned FULL = 0xffffffffu;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (n % (16 * K) != 0 || n < 32 * K) {
+        __syncthreads();
+        if (tid == 0) answer = chain_sum(0.0f, v, n);
+        __syncthreads();
+        if (hit) *hit = 0;
+        return answer;
+    }
+    const int m = n / K;
+    // exact sums of segments 0..K-2, estimated in double (same order in every thread)
+    double d[NB];
+#pragma unroll
+    for (int k = 0; k < NB; k++) d[k] = 0.0;
+    for (int i = tid; i < m; i += NT) {
+#pragma unroll
+        for (int k = 0; k < NB; k++) d[k] = __dadd_rn(d[k], (double)v[k * m + i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int k = 0; k < NB; k++) d[k] = __dadd_rn(d[k], __shfl_down_sync(FULL, d[k], o));
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int k = 0; k < NB; k++) red[k][warp] = d[k];
+    }
+    __syncthreads();
+    // window starts b0[k] for the sum of segments 0..k (the start of segment k+1)
+    uint32_t b0[NB];
+    bool finite = true;
+    double D = 0.0;
+#pragma unroll
+    for (int k = 0; k < NB; k++) {
+#pragma unroll
+        for (int w = 0; w < NT / 32; w++) D = __dadd_rn(D, red[k][w]);
+        const uint32_t bc = __float_as_uint(__double2float_rn(D));
+        finite = finite && bc < 0x7F000000u;
+        b0[k] = bc > NC / 2 ? bc - NC / 2 : 0u;
+    }
+    if (tid <= NC * NB) {
+        const bool is_first = tid == NC * NB;
+        const int kk = is_first ? 0 : tid / NC, j = tid % NC;
+        uint32_t mine = b0[0];
+#pragma unroll
+        for (int k = 1; k < NB; k++) mine = kk == k ? b0[k] : mine;
+        float s = is_first ? 0.0f : __uint_as_float(mine + (uint32_t)j);
+        const float4 *src = reinterpret_cast<const float4 *>(v + (is_first ? 0 : (kk + 1) * m));
+        const int q = m / 4;
+        float4 c0 = src[0], c1 = src[1], c2 = src[2], c3 = src[3];
+#define EMB_ADD4(c)                                                       \
+    s = __fadd_rn(s, c.x); s = __fadd_rn(s, c.y); s = __fadd_rn(s, c.z); \
+    s = __fadd_rn(s, c.w);
+        for (int k = 4; k < q; k += 4) {
+            const float4 n0 = src[k], n1 = src[k + 1], n2 = src[k + 2], n3 = src[k + 3];
+            EMB_ADD4(c0) EMB_ADD4(c1) EMB_ADD4(c2) EMB_ADD4(c3)
+            c0 = n0; c1 = n1; c2 = n2; c3 = n3;
+        }
+        EMB_ADD4(c0) EMB_ADD4(c1) EMB_ADD4(c2) EMB_ADD4(c3)
+#undef EMB_ADD4
+        if (is_first) first_part = s;
+        else cand[kk][j] = s;
+    }
+    __syncthreads();
+    // walk the boundaries: s = the float sum of segments 0..k
+    float s = first_part;
+    int done = 1;   // segments summed into s
+#pragma unroll
+    for (int k = 0; k < NB; k++) {
+        const uint32_t jk = __float_as_uint(s) - b0[k];
+        if (done == k + 1 && finite && jk < (uint32_t)NC) {
+            s = cand[k][jk];
+            done = k + 2;
+        }
+    }
+    if (hit) *hit = done == K;
+    if (done == K) return s;
+    if (tid == 0) answer = chain_sum(s, v + done * m, n - done * m);
+    __syncthreads();
+    return answer;
+}
+
 // ---- bulk async copies (TMA, non-tensor form) and mbarriers ----------------
 EMB_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

@@ -83,12 +83,11 @@ __host__ __device__ inline size_t gemv_sub_bytes(int dtype, int rows, int cols) 
 }
 
 // bytes of the region that holds the tile products P, and during an RMSNorm
-// prologue (before any tile) the norm weights, the squares and the exact-sum
-// scratch instead
+// prologue (before any tile) the norm weights and the squares instead
 __host__ __device__ inline size_t gemv_p_bytes(int cols, bool in_norm) {
     size_t p = (size_t)2 * GEMV_MAX_ROWS * gemv_p_stride(cols / 32) * 4;
-    size_t pro = (size_t)cols * 4;   // the prologue's norm weights (in_norm)
-    (void)in_norm;
+    // the prologue's norm weights and squares (in_norm)
+    size_t pro = in_norm ? (size_t)cols * 8 : 0;
     return pad16(p > pro ? p : pro);
 }
 
@@ -197,7 +196,6 @@ template <int IN, int EPI>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[GEMV_MAX_STAGES];
-    __shared__ float s_scale;
     __shared__ double tab_s[EPI == EPI_SWIGLU ? 64 : 1];
     constexpr int nsub = EPI == EPI_SWIGLU ? 2 : 1;
     const int tid = threadIdx.x, R = a.rows;
@@ -247,16 +245,24 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
         if (need_xf)
             for (int i = tid; i < cols; i += GEMV_THREADS) xf_s[i] = a.xf[i];
     } else {
-        for (int i = tid; i < cols; i += GEMV_THREADS) xf_s[i] = a.x[i];
+        // RMSNorm (ref src/model.c:50-55): the sum of squares in index order, as
+        // the reference adds, by split_chain_sum over the squares (after the norm
+        // weights in the prologue scratch)
+        float *sq_s = nw_s + cols;
         if (IN == IN_NORM) {
-            // RMSNorm (ref src/model.c:50-55): the sum of squares as ONE sequential
-            // chain in index order, as the reference adds
+            for (int i = tid; i < cols; i += GEMV_THREADS) {
+                const float v = a.x[i];
+                xf_s[i] = v;
+                sq_s[i] = fmul(v, v);
+            }
+        } else {
+            for (int i = tid; i < cols; i += GEMV_THREADS) xf_s[i] = a.x[i];
+        }
+        if (IN == IN_NORM) {
             __syncthreads();
             EMB_PROBE(PK, 3);
-            if (tid == 0) s_scale = rms_scale(chain_sumsq(xf_s, cols), cols, a.eps);
-            __syncthreads();
+            const float sc = rms_scale(split_chain_sum<GEMV_THREADS>(sq_s, cols), cols, a.eps);
             EMB_PROBE(PK, 4);
-            const float sc = s_scale;
             for (int i = tid; i < cols; i += GEMV_THREADS)
                 xf_s[i] = fmul(fmul(xf_s[i], sc), nw_s[i]);   // (x*scale)*w
         }

@@ -170,6 +170,12 @@ int          ember_cuda_available(void);
 int  ember_host_expf_params(EmberExpfParams *out);
 /* the device recipe evaluated on the host (identical bits); for tests */
 float ember_host_expf_emulated(const EmberExpfParams *p, float x);
+/* The decode GEMVs' RMSNorm sum (split_chain_sum) on `count` vectors of n
+ * non-negative terms each (host arrays, n <= 32768): host_out[i] = the terms
+ * added in index order from 0, host_hit[i] = 1 where the split evaluation
+ * answered (0: the second half was added after the first). 0 on success. For
+ * tests. */
+int ember_cuda_split_sum_batch(const float *host_terms, int n, int count, float *host_out, int *host_hit);
 /* fills [ctx][hd/2][2] with the reference's cos/sin values */
 void ember_host_rope_table(float *out, int ctx, int head_dim, float theta);
 
