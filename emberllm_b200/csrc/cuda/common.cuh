@@ -104,6 +104,16 @@ __host__ __device__ inline size_t qrow_bytes(int dtype, int cols) {
 // pre-wait work of a kernel may read weights, tables, and anything written two
 // or more launches earlier (the KV cache of previous positions, the step's
 // position word), and must not read what its immediate predecessor writes.
+// 16-byte global -> shared copies that complete asynchronously (cp.async):
+// issue, commit the group, and wait for all groups before reading the data
+EMB_DEV void cp_async16(void *smem_dst, const void *gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+                 "l"(gmem_src)
+                 : "memory");
+}
+EMB_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+EMB_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 EMB_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 EMB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 

@@ -412,32 +412,21 @@ struct AttnArgs {
 
 
 // Copy keys of positions [c0, c0+n) (all hd rows of the transposed layout) into
-// kbuf[hd][CH] with 16-byte loads by all threads, eight in flight per thread.
-// Rows are padded to kstride, so rounding n up to a vector stays in bounds.
+// kbuf[hd][CH] with 16-byte asynchronous copies by all threads. Rows are padded
+// to kstride, so rounding n up to a vector stays in bounds; positions from n on
+// (the current one included, which this launch writes) are copied but not read.
 template <typename T>
 EMB_DEV void load_k_chunk(T *kbuf, const T *kt, int kstride, int c0, int n, int hd, int CH) {
+    // 16-byte cp.async copies, all in flight at once; the caller waits
+    // (cp_async_wait_all + __syncthreads) before reading kbuf
     constexpr int E = 16 / (int)sizeof(T);
     const int nv = (n + E - 1) / E;
     const int total = hd * nv;
-    for (int base = threadIdx.x; base < total; base += ATTN_THREADS * 8) {
-        int4 r[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int idx = base + u * ATTN_THREADS;
-            if (idx < total) {
-                const int i = idx / nv, vv = idx - i * nv;
-                r[u] = *reinterpret_cast<const int4 *>(kt + (size_t)i * kstride + c0 + vv * E);
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int idx = base + u * ATTN_THREADS;
-            if (idx < total) {
-                const int i = idx / nv, vv = idx - i * nv;
-                *reinterpret_cast<int4 *>(kbuf + (size_t)i * CH + vv * E) = r[u];
-            }
-        }
+    for (int idx = threadIdx.x; idx < total; idx += ATTN_THREADS) {
+        const int i = idx / nv, vv = idx - i * nv;
+        cp_async16(kbuf + (size_t)i * CH + vv * E, kt + (size_t)i * kstride + c0 + vv * E);
     }
+    cp_async_commit();
 }
 
 // One query position over the cache for one head (ref src/model.c:221-259).
@@ -495,7 +484,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
         mbar_expect_tx(&bars[1], (uint32_t)(n0 * hd * (int)sizeof(T)));
         bulk_g2s(buf1, vt, (uint32_t)(n0 * hd * sizeof(T)), &bars[1]);
     }
-    if (n0 > 0) load_k_chunk(buf0, kt, a.kstride, 0, n0, hd, CH);   // keys of chunk 0 -> buf0
+    if (n0 > 0) load_k_chunk(buf0, kt, a.kstride, 0, n0, hd, CH);   // keys of chunk 0 -> buf0 (async)
     EMB_PROBE(4, 1);
     pdl_wait_then_release();
     EMB_PROBE(4, 2);
@@ -546,6 +535,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
             vt[(size_t)pos * hd + tid] = vq;
         }
     }
+    cp_async_wait_all();   // the keys of chunk 0, copied since before the wait
     __syncthreads();
 
     EMB_PROBE(4, 5);
@@ -556,6 +546,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
         if (c > 0) {
             __syncthreads();
             load_k_chunk(buf0, kt, a.kstride, c0, n, hd, CH);
+            cp_async_wait_all();
             __syncthreads();
         }
         for (int t = tid; t < n; t += ATTN_THREADS) {

@@ -399,8 +399,10 @@ static GemvSeg seg_of(const DevMat &d, float *out, const float *bias) {
 
 // Choose the tile height, ring depth and grid of one gemv launch and launch it.
 // Segments must agree on being quantized (callers split otherwise).
+// max_ctas > 0 caps the grid of a non-persistent launch (taller tiles) so that
+// SMs stay free for the next kernel's CTAs to start early.
 template <int IN, int EPI>
-static int run_gemv(GemvArgs a, int n_sm, cudaStream_t st, int *count) {
+static int run_gemv(GemvArgs a, int n_sm, cudaStream_t st, int *count, int max_ctas = 0) {
     const int nsub = EPI == EPI_SWIGLU ? 2 : 1;
     a.quantized = a.seg[0].dtype != EMBER_DT_F32;
     int rows_total = 0;
@@ -408,8 +410,10 @@ static int run_gemv(GemvArgs a, int n_sm, cudaStream_t st, int *count) {
     // SwiGLU tiles are one quant block of h (32 rows); others shrink to spread
     // small matrices over more SMs (R >= 8 keeps scale copies 16-byte aligned)
     int R = GEMV_MAX_ROWS;
-    if (EPI != EPI_SWIGLU)
+    if (EPI != EPI_SWIGLU) {
         while (R > 8 && (rows_total + R - 1) / R < n_sm) R /= 2;
+        while (max_ctas > 0 && R < GEMV_MAX_ROWS && (rows_total + R - 1) / R > max_ctas) R *= 2;
+    }
     a.rows = R;
     if (EPI == EPI_SWIGLU) {
         a.tiles[0] = 0;
@@ -502,7 +506,10 @@ static int launch_layer(EmberCudaState *s, int kind, int l, int *count) {
             a.seg[1] = seg_of(L.wk, s->k, L.bk);
             a.seg[2] = seg_of(L.wv, s->v, L.bv);
             a.nseg = 3;
-            return run_gemv<IN_NORM, EPI_STORE>(a, m->n_sm, st, count);
+            // the single-kernel attention that follows needs whole SMs (large
+            // key/value buffers): leave one free per query head
+            return run_gemv<IN_NORM, EPI_STORE>(a, m->n_sm, st, count,
+                                                s->attn_split ? 0 : m->n_sm - m->n_heads);
         } else {
             const DevMat *mats[3] = { &L.wq, &L.wk, &L.wv };
             float *outs[3] = { s->q, s->k, s->v };
