@@ -61,7 +61,7 @@ struct AttnSplitArgs {
 // dynamic shared memory of the two kernels
 __host__ __device__ inline size_t as_scores_smem(int hd, int es) { return (size_t)hd * AS_PER * es; }
 __host__ __device__ inline size_t as_pv_smem(int kv_mul, int ctx, int es, int w_smem) {
-    return (size_t)AS_VSTAGES * AS_VB * 32 * es + (w_smem ? (size_t)kv_mul * ((ctx + 3) / 4 * 4) * 4 : 0);
+    return (size_t)AS_VSTAGES * AS_VB * 32 * es + (w_smem ? (size_t)kv_mul * ((ctx + 63) / 64 * 64) * 4 : 0);
 }
 
 // 2-D TMA load of a box at (x, y) completing on `bar` (no multicast)
@@ -291,19 +291,26 @@ __global__ void __launch_bounds__(AS_THREADS) attn_softmax_pv_kernel(const __gri
         }
         __syncthreads();
     }
+    // (and zeros up to a multiple of 64 positions: trailing +0 terms leave the
+    // sums unchanged; the row stride is a multiple of 64)
+    const int Ppad = (P + 63) / 64 * 64;
     for (int r = 0; r < kv_mul; r++) {
         const float mx = s_max[r];
         float *wr = ws + (size_t)r * wst;
         const float *sr = WS ? wr : sc + (size_t)r * a.ast;
-        for (int t = tid; t < P; t += AS_THREADS) wr[t] = expf_exact(a.ex, tab_s, fsub(sr[t], mx));
+        for (int t = tid; t < Ppad; t += AS_THREADS) wr[t] = t < P ? expf_exact(a.ex, tab_s, fsub(sr[t], mx)) : 0.0f;
     }
     __syncthreads();
     EMB_PROBE(7, 4);
-    // denominators: the sequential sum over t (ref src/model.c:61), one chain per head
+    // denominators: the sequential sum over t (ref src/model.c:61), head by head,
+    // each by the whole block (split_chain_sum)
 #ifdef EMBER_PROBES
     const long long c0 = clock64();
 #endif
-    if (lane == 0 && warp < kv_mul) s_inv[warp] = fdiv(1.0f, chain_sum_pipe(0.0f, ws + (size_t)warp * wst, P));
+    for (int r = 0; r < kv_mul; r++) {
+        const float den = split_chain_sum<AS_THREADS>(ws + (size_t)r * wst, Ppad);
+        if (tid == 0) s_inv[r] = fdiv(1.0f, den);
+    }
 #ifdef EMBER_PROBES
     if (blockIdx.x == 0 && tid == 0) g_probe[7][10] = (unsigned long long)(clock64() - c0);
 #endif

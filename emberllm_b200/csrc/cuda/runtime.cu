@@ -276,7 +276,7 @@ extern "C" int ember_cuda_state_new(EmberCudaModel *m, int ctx, int kv_fp16, con
                     (force_split || ctx > 512);
     s->attn_splits = (ctx + AS_PER - 1) / AS_PER;
     s->attn_w_smem = as_pv_smem(m->n_heads / m->n_kv, ctx, (int)es, 1) <= 200 * 1024;
-    s->att_stride = (ctx + 3) / 4 * 4;
+    s->att_stride = (ctx + 63) / 64 * 64;   // split_chain_sum pads rows to 64 positions
     rc |= salloc(s, (void **)&s->att, (size_t)m->n_heads * s->att_stride * 4 + 256);
     if (s->attn_split && !s->attn_w_smem)
         rc |= salloc(s, (void **)&s->wglob, (size_t)(hd / 32) * m->n_heads * s->att_stride * 4 + 256);
