@@ -321,9 +321,12 @@ def run_streams(args, world, rank, local, dist):
     clocks = ClockSampler(local)
     clocks.start()
     barrier(dist)
+    nvtx = Nvtx(args.nvtx)
     t0 = time.perf_counter()
+    nvtx.push("streams")
     for _ in range(args.steps):
         b.greedy(firsts, pos, ntok)     # synchronous: tokens come back to the host
+    nvtx.pop()
     t = time.perf_counter() - t0
     clk = clocks.stop()
     t_max = max_over_ranks(dist, t)
