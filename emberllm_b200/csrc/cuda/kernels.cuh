@@ -233,6 +233,14 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
     if (IN == IN_NORM)
         for (int i = tid; i < cols; i += GEMV_THREADS) nw_s[i] = a.norm_w[i];
     if (EPI == EPI_SWIGLU) expf_table_load(tab_s, a.ex);
+    // residual rows of the first tile: x was last written two or more launches
+    // back (w2 of the previous layer before wo; wo before w13, w2), so it may be
+    // read before the wait
+    float resid0 = 0.0f;
+    if (EPI == EPI_RESID && my_tiles > 0 && tid < R) {
+        const TileRef t0 = tile_ref<EPI>(a, blockIdx.x, 0);
+        if (tid < t0.nrows) resid0 = t0.g.out[t0.row0 + tid];
+    }
     EMB_PROBE(PK, 1);
     pdl_wait_then_release();
     EMB_PROBE(PK, 2);
@@ -379,7 +387,8 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
             float s = rowsum[tid];
             const GemvSeg &g = tr[0].g;
             if (EPI == EPI_RESID) {
-                g.out[row0 + tid] = fadd(g.out[row0 + tid], s);    // x += y (ref :398, :408)
+                const float x = k == 0 ? resid0 : g.out[row0 + tid];
+                g.out[row0 + tid] = fadd(x, s);    // x += y (ref :398, :408)
             } else {
                 if (g.bias) s = fadd(s, g.bias[row0 + tid]);
                 g.out[row0 + tid] = s;
