@@ -341,7 +341,10 @@ def run_streams(args, world, rank, local, dist):
         "dtype": "int8 dot / fp32 (Q8_0 weights, exact reference arithmetic)",
         "data": "synthetic: N(0,0.02) weights seed 0, per-stream uniform random prompts",
         "config": {"workload": "%d streams (8 x %d), 256-token prompts, %d greedy tokens each, decoded "
-                               "together per GPU" % (total, args.streams, ntok),
+                               "together per GPU (%s)" % (total, args.streams, ntok,
+                                                          "concurrent single-stream states" if S <= 8 and
+                                                          os.environ.get("EMBER_BATCH") != "gemm"
+                                                          else "batched tcgen05 GEMMs"),
                    "model": args.config, "streams": total, "streams_per_gpu": S, "tokens_per_step": ntok,
                    "parallelism": "streams split over %d GPU(s), one replica each" % world},
         "per_stream_tok_s": round(value / total, 2),

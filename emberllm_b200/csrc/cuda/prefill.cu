@@ -610,7 +610,17 @@ struct EmberCudaBatch {
     PfState *ps = nullptr;
     cudaGraphExec_t g_step = nullptr;
     std::vector<void *> allocs;
+    // few streams: one single-stream state per stream, their greedy graphs
+    // running at once on their own CUDA streams (a handful of one-token steps
+    // overlap better than a GEMM of a handful of rows)
+    std::vector<EmberCudaState *> reps;
+    int *htok = nullptr;                  // pinned [S][max_steps] chosen tokens
 };
+
+// streams up to which a batch keeps one single-stream state per stream (the
+// default number of hardware work queues); EMBER_BATCH=gemm forces the batched
+// GEMM path at any size
+constexpr int BATCH_REPLICA_MAX = 8;
 
 static void batch_release(EmberCudaBatch *b) {
     if (b->g_step) cudaGraphExecDestroy(b->g_step);
@@ -618,6 +628,10 @@ static void batch_release(EmberCudaBatch *b) {
     for (void *p : b->allocs) cudaFree(p);
     b->allocs.clear();
     if (b->worker) ember_cuda_state_free(b->worker);
+    for (EmberCudaState *r : b->reps) ember_cuda_state_free(r);
+    b->reps.clear();
+    if (b->htok) cudaFreeHost(b->htok);
+    b->htok = nullptr;
 }
 
 extern "C" int ember_cuda_batch_new(EmberCudaModel *m, int n_streams, int ctx, int kv_fp16, const float *rope_cs,
@@ -629,6 +643,25 @@ extern "C" int ember_cuda_batch_new(EmberCudaModel *m, int n_streams, int ctx, i
     if (!pf_supported(m)) return set_err("batch: the model's layer weights are not all Q8_0 / Q4_0");
     EmberCudaBatch *b = new EmberCudaBatch();
     b->m = m; b->S = n_streams; b->ctx = ctx; b->kv_fp16 = kv_fp16 ? 1 : 0; b->max_steps = max_steps;
+    const char *mode = getenv("EMBER_BATCH");
+    if (n_streams <= BATCH_REPLICA_MAX && !(mode && strcmp(mode, "gemm") == 0)) {
+        int rc = cudaMallocHost((void **)&b->htok, (size_t)n_streams * max_steps * 4) != cudaSuccess
+                     ? set_err("batch: pinned token buffer allocation failed")
+                     : 0;
+        for (int i = 0; i < n_streams && !rc; i++) {
+            EmberCudaState *r = nullptr;
+            rc = ember_cuda_state_new(m, ctx, b->kv_fp16, rope_cs, &r);
+            if (!rc) b->reps.push_back(r);
+            if (!rc) rc = greedy_prepare(r);
+        }
+        if (rc) {
+            batch_release(b);
+            delete b;
+            return 1;
+        }
+        *out = b;
+        return 0;
+    }
     int rc = ember_cuda_state_new(m, ctx, b->kv_fp16, rope_cs, &b->worker);
     if (!rc) rc = pf_prepare_model(m) || pf_init(m->device) || pf_prepare_head(m);
     const size_t es = b->kv_fp16 ? 2 : 4;
@@ -667,12 +700,15 @@ extern "C" int ember_cuda_batch_new(EmberCudaModel *m, int n_streams, int ctx, i
 extern "C" void ember_cuda_batch_free(EmberCudaBatch *b) {
     if (!b) return;
     cudaSetDevice(b->m->device);
-    cudaStreamSynchronize(b->worker ? b->worker->stream : nullptr);
+    if (b->worker) cudaStreamSynchronize(b->worker->stream);
+    for (EmberCudaState *r : b->reps) cudaStreamSynchronize(r->stream);
     batch_release(b);
     delete b;
 }
 
-extern "C" void *ember_cuda_batch_stream(EmberCudaBatch *b) { return (void *)b->worker->stream; }
+extern "C" void *ember_cuda_batch_stream(EmberCudaBatch *b) {
+    return (void *)(b->worker ? b->worker->stream : b->reps[0]->stream);
+}
 
 // the worker state's cache pointers aimed at stream i's cache
 static void aim_worker(EmberCudaBatch *b, int i) {
@@ -685,6 +721,7 @@ extern "C" int ember_cuda_batch_prefill(EmberCudaBatch *b, int stream, const int
     CK(cudaSetDevice(b->m->device));
     if (stream < 0 || stream >= b->S) return set_err("batch: stream %d out of range", stream);
     if (n < 1 || n > b->ctx) return set_err("batch: prompt of %d tokens does not fit the context", n);
+    if (!b->reps.empty()) return ember_cuda_prefill(b->reps[stream], ids, n, 0, host_logits);
     EmberCudaState *w = b->worker;
     aim_worker(b, stream);
     // the batched prefill (also for one token: the decode graphs of the worker
@@ -733,6 +770,22 @@ extern "C" int ember_cuda_batch_greedy(EmberCudaBatch *b, const int *toks, const
     for (int i = 0; i < b->S; i++) {
         if (toks[i] < 0 || toks[i] >= b->m->vocab) return set_err("batch: token id %d out of range", toks[i]);
         if (pos[i] < 0 || pos[i] + n_steps > b->ctx) return set_err("batch: stream %d does not fit the context", i);
+    }
+    if (!b->reps.empty()) {
+        // every stream's steps enqueued before any wait, so that they run at once
+        for (int i = 0; i < b->S; i++)
+            if (greedy_enqueue(b->reps[i], toks[i], pos[i], n_steps, b->htok + (size_t)i * b->max_steps)) return 1;
+        int rc = 0;
+        for (int i = 0; i < b->S; i++) rc |= greedy_finish(b->reps[i]);
+        if (rc) return 1;
+        if (host_tokens)
+            for (int t = 0; t < n_steps; t++)
+                for (int i = 0; i < b->S; i++) host_tokens[(size_t)t * b->S + i] = b->htok[(size_t)i * b->max_steps + t];
+        if (host_logits)
+            for (int i = 0; i < b->S; i++)
+                CK(cudaMemcpy(host_logits + (size_t)i * b->m->vocab, b->reps[i]->logits, (size_t)b->m->vocab * 4,
+                              cudaMemcpyDeviceToHost));
+        return 0;
     }
     cudaStream_t st = b->worker->stream;
     if (!b->g_step) {

@@ -768,20 +768,40 @@ int ember_cuda_prefill_batched(EmberCudaState *s, const int *ids, int n, int sta
     return prefill_impl(s, ids, n, start, host_logits, true);
 }
 
-extern "C" int ember_cuda_greedy(EmberCudaState *s, int tok, int pos, int n_steps, int *host_tokens,
-                                 float *host_logits) {
+// the state's greedy-step graph, captured once
+int emb::greedy_prepare(EmberCudaState *s) {
     CK(cudaSetDevice(s->m->device));
-    if (n_steps <= 0) return 0;
-    if (!s->g_greedy && capture(s, &s->g_greedy, 1)) return 1;
+    return !s->g_greedy && capture(s, &s->g_greedy, 1);
+}
+
+// Enqueue n_steps greedy steps on the state's stream without waiting: step i
+// feeds t_i at pos + i (t_0 = tok); the chosen tokens go to host_tokens (pinned
+// memory, or the copy synchronises) once the steps are done.
+int emb::greedy_enqueue(EmberCudaState *s, int tok, int pos, int n_steps, int *host_tokens) {
+    if (greedy_prepare(s)) return 1;
     int *hc = s->h_ctl;
     CK(cudaStreamSynchronize(s->stream));
     hc[CTL_POS] = pos; hc[CTL_TOK] = tok; hc[CTL_NOUT] = 0; hc[CTL_BASE] = 0; hc[CTL_ERR] = 0;
     CK(cudaMemcpyAsync(s->ctl, hc, 5 * sizeof(int), cudaMemcpyHostToDevice, s->stream));
     for (int i = 0; i < n_steps; i++) CK(cudaGraphLaunch(s->g_greedy, s->stream));
     if (host_tokens) CK(cudaMemcpyAsync(host_tokens, s->out_tokens, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, s->stream));
-    if (host_logits) CK(cudaMemcpyAsync(host_logits, s->logits, (size_t)s->m->vocab * 4, cudaMemcpyDeviceToHost, s->stream));
+    return 0;
+}
+
+// wait for the state's enqueued work and report a device-side error
+int emb::greedy_finish(EmberCudaState *s) {
+    CK(cudaSetDevice(s->m->device));
     CK(cudaStreamSynchronize(s->stream));
     return read_error_word(s);
+}
+
+extern "C" int ember_cuda_greedy(EmberCudaState *s, int tok, int pos, int n_steps, int *host_tokens,
+                                 float *host_logits) {
+    CK(cudaSetDevice(s->m->device));
+    if (n_steps <= 0) return 0;
+    if (greedy_enqueue(s, tok, pos, n_steps, host_tokens)) return 1;
+    if (host_logits) CK(cudaMemcpyAsync(host_logits, s->logits, (size_t)s->m->vocab * 4, cudaMemcpyDeviceToHost, s->stream));
+    return greedy_finish(s);
 }
 
 extern "C" int ember_cuda_profile_step(EmberCudaState *s, int tok, int pos, float *ms_out, int cap,

@@ -109,6 +109,12 @@ static inline int salloc(EmberCudaState *s, void **p, size_t n) {
 
 // ember_cuda_prefill that always takes the batched path (also for one token)
 int ember_cuda_prefill_batched(EmberCudaState *s, const int *ids, int n, int start, float *host_logits);
+namespace emb {
+// greedy decoding on a state's stream, split so that several states can run at once
+int greedy_prepare(EmberCudaState *s);
+int greedy_enqueue(EmberCudaState *s, int tok, int pos, int n_steps, int *host_tokens);
+int greedy_finish(EmberCudaState *s);
+}  // namespace emb
 
 // ---- batched prefill (prefill.cu) ----
 namespace emb {

@@ -1,11 +1,13 @@
 """GPU parity of the batched decode of independent streams (ember_batch_*).
 
 BASELINE's many-sequence workload runs 8 x N independent streams, each with its
-own prompt and greedy continuation. The library decodes them together (one
-tensor-core GEMM per weight matrix per step, each stream at its own position in
-its own cache); per stream the arithmetic is the single-sequence step's, so
-every stream must produce exactly the tokens of its own greedy run, and the last
-step's logits must equal the oracle's bit for bit.
+own prompt and greedy continuation. The library decodes up to 8 streams as
+concurrent single-stream states (their step graphs on separate CUDA streams) and
+more streams together (one tensor-core GEMM per weight matrix per step, each
+stream at its own position in its own cache). Either way the arithmetic per
+stream is the single-sequence step's, so every stream must produce exactly the
+tokens of its own greedy run, and the last step's logits must equal the oracle's
+bit for bit.
 """
 import numpy as np
 import pytest
@@ -51,10 +53,17 @@ def run_batch(path, prompts, n_steps, kv16, ctx):
     return firsts, toks, logits
 
 
+@pytest.mark.parametrize("mode", ["replicas", "gemm"])
 @pytest.mark.parametrize("kv16", [0, 1])
 @pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen3", "tiny-qwen2", "tiny-smol-q4", "tiny-mqa"])
-def test_tiny_streams_match_single_sequence_runs(orc, name, kv16):
-    """five streams with prompts of 1..30 tokens, 12 steps together"""
+def test_tiny_streams_match_single_sequence_runs(orc, name, kv16, mode, monkeypatch):
+    """five streams with prompts of 1..30 tokens, 12 steps together; up to 8
+    streams run as concurrent single-stream states unless EMBER_BATCH=gemm
+    forces the batched GEMM path"""
+    if mode == "gemm":
+        monkeypatch.setenv("EMBER_BATCH", "gemm")
+    else:
+        monkeypatch.delenv("EMBER_BATCH", raising=False)
     path = synth.ensure_model(name)
     vocab = H.header_of(path)["vocab_size"]
     rng = np.random.default_rng(31 + kv16)
@@ -69,9 +78,14 @@ def test_tiny_streams_match_single_sequence_runs(orc, name, kv16):
 
 
 @pytest.mark.slow
-def test_qwen3_eight_streams(orc):
+@pytest.mark.parametrize("mode", ["replicas", "gemm"])
+def test_qwen3_eight_streams(orc, mode, monkeypatch):
     """the BASELINE streams architecture at full size: 8 streams (configs[4],
-    N = 1), 32-token prompts, 16 steps"""
+    N = 1), 32-token prompts, 16 steps, on both batch paths"""
+    if mode == "gemm":
+        monkeypatch.setenv("EMBER_BATCH", "gemm")
+    else:
+        monkeypatch.delenv("EMBER_BATCH", raising=False)
     path = synth.ensure_model("qwen3-0.6b")
     rng = np.random.default_rng(4)
     vocab = H.header_of(path)["vocab_size"]
