@@ -64,7 +64,7 @@ __host__ __device__ inline size_t as_pv_smem(int kv_mul, int ctx, int es, int w_
     return (size_t)AS_VSTAGES * AS_VB * 32 * es + (w_smem ? (size_t)kv_mul * ((ctx + 63) / 64 * 64) * 4 : 0);
 }
 
-// 2-D TMA load of a box at (x, y) completing on `bar` (no multicast)
+// 2-D TMA load of a box at (x, y) into this CTA only, completing on `bar`
 EMB_DEV void as_tma_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(

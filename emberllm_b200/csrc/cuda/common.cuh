@@ -343,7 +343,7 @@ EMB_DEV void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
 }
 
 // global -> shared bulk copy completing on `bar`; dst, src 16-byte aligned,
-// bytes a multiple of 16. No multicast.
+// bytes a multiple of 16; the copy lands in this CTA only.
 EMB_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

@@ -79,7 +79,7 @@ EMB_DEV bool pf_wait(uint64_t *bar, uint32_t parity, int *err, volatile int *abo
     return true;
 }
 
-// 2-D tiled TMA load (no multicast): box at (x = inner element, y = row)
+// 2-D tiled TMA load into this CTA only: box at (x = inner element, y = row)
 EMB_DEV void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
