@@ -132,12 +132,16 @@ int  ember_cuda_argmax_static(const float *logits, int n, int *out_index, void *
 /* ---- batched greedy decode of independent streams ----
  * No counterpart in the reference (which decodes one sequence per state); this
  * is the many-sequence workload: n_streams independent sequences, each with its
- * own KV cache of ctx positions, advanced together. Every step runs all streams'
- * tokens through the layers as one batch (tensor-core GEMMs over the streams),
- * each at its own position, then the final norm, lm_head and a per-stream greedy
- * pick. Per stream the arithmetic is the single-sequence step's, so each
- * stream's tokens and logits equal those of its own ember_forward run.
- * Requires Q8_0/Q4_0 layer and lm_head weights; n_streams in [1, 512]. */
+ * own KV cache of ctx positions, advanced together. Up to 8 streams, the batch
+ * holds one single-stream state per stream and runs their greedy steps at once
+ * on separate CUDA streams. Beyond that (or with EMBER_BATCH=gemm), every step
+ * runs all streams' tokens through the layers as one batch (tensor-core GEMMs
+ * over the streams), each at its own position, then the final norm, lm_head and
+ * a per-stream greedy pick. Per stream the arithmetic is the single-sequence
+ * step's, so each stream's tokens and logits equal those of its own
+ * ember_forward run. Requires Q8_0/Q4_0 layer and lm_head weights; n_streams in
+ * [1, 512]. ember_cuda_batch_stream returns the stream of the batch (of its first
+ * state when the batch holds one per stream). */
 typedef struct EmberCudaBatch EmberCudaBatch;
 int  ember_cuda_batch_new(EmberCudaModel *m, int n_streams, int ctx, int kv_fp16, const float *rope_cs,
                           int max_steps, EmberCudaBatch **out);
