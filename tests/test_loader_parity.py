@@ -119,3 +119,35 @@ def test_missing_file_and_unknown_tensor(tmp_path):
     ours = run(OURS, path, "layers.7.wq")
     assert ours == run(REF, path, "layers.7.wq")
     assert ours[0] == "loaded True\ntensor False\n"
+
+
+STATE_SNIPPET = r"""
+import ctypes, sys
+lib = ctypes.CDLL(sys.argv[1])
+lib.ember_model_load.restype = ctypes.c_void_p
+lib.ember_state_new.restype = ctypes.c_void_p
+lib.ember_state_new.argtypes = [ctypes.c_void_p, ctypes.c_int]
+m = lib.ember_model_load(sys.argv[2].encode())
+print("loaded", bool(m), flush=True)
+lib.ember_state_new(m, 64)
+"""
+
+
+@pytest.mark.parametrize("model,tensor", [("tiny-llama", "layers.1.wq"), ("tiny-llama", "final_norm"),
+                                          ("tiny-llama", "tok_embeddings"), ("tiny-qwen3", "layers.0.attn_norm"),
+                                          ("tiny-qwen3", "layers.1.w2")])
+def test_missing_tensor_dies_like_the_reference(tmp_path, model, tensor):
+    """ref src/model.c:161-171: state creation resolves every tensor and dies with
+    the reference's message on the first one missing (here before any device work)"""
+    good = open(synth.ensure_model(model), "rb").read()
+    at = table_entry_offset(good, tensor)
+    bad = good[:at] + b"missing_" + good[at + 8:]     # rename the entry
+    p = tmp_path / "missing.ember"
+    p.write_bytes(bad)
+    got = {}
+    for lib in (OURS, REF):
+        r = subprocess.run([sys.executable, "-c", STATE_SNIPPET, lib, str(p)], capture_output=True, text=True,
+                           timeout=120)
+        got[lib] = (r.returncode, r.stdout, r.stderr)
+    assert got[OURS] == got[REF], got
+    assert got[OURS][0] == 1 and got[OURS][2].startswith("ember: ")
