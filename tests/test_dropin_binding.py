@@ -1,8 +1,10 @@
-"""The drop-in recipe of INTEGRATION.md, checked on CPU: emberllm's own front-end
+"""The drop-in recipes of INTEGRATION.md, checked on CPU. emberllm's own front-end
 sources (tokenizer, sampler, JSON, server) link against this library into a
 `libember.so`, and emberllm's unmodified Python binding (bindings/python/
-emberllm.py) loads it through EMBER_LIB and works: model header and tokenizer
-round trip equal to the same binding over the reference's own build. (State
+emberllm.py) loads it through EMBER_LIB: model header and tokenizer round trip
+equal the same binding over the reference's own build. emberllm's CLI
+(main.c + the same front ends) links against this library too: `info`,
+`tokenize` and `quantize` print and write what the reference's CLI does. (State
 creation and the token loop need the GPU; the GPU tests cover them.)"""
 import json
 import os
@@ -66,3 +68,49 @@ def test_reference_binding_runs_on_the_dropin_library(dropin, name):
     ours, ref = probe(dropin, model, text), probe(REF_LIB, model, text)
     assert ours == ref
     assert len(ours["ids"]) > 1
+
+
+@pytest.fixture(scope="module")
+def cli(tmp_path_factory):
+    """emberllm's CLI linked as INTEGRATION.md's Makefile does: its front-end
+    sources and this library"""
+    out = tmp_path_factory.mktemp("cli") / "ember"
+    src = [os.path.join(REF_SRC, "src", f) for f in ("main.c", "tokenizer.c", "sample.c", "json.c", "server.c")]
+    r = subprocess.run(["gcc", "-std=c11", "-D_DEFAULT_SOURCE", "-O2", "-o", str(out), *src, "-L" + B200,
+                        "-lember_b200", "-Wl,-rpath," + B200, "-lm", "-lpthread"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    return str(out)
+
+
+def ref_cli():
+    path = os.path.join(ROOT, "oracle", "_ref", "ember_ref_v3")
+    if not os.path.exists(path):
+        pytest.skip("the reference CLI (oracle/_ref) was not built")
+    return path
+
+
+def run_cli(binary, *args):
+    r = subprocess.run([binary, *args], capture_output=True, text=True, timeout=300)
+    return r.returncode, r.stdout
+
+
+@pytest.mark.parametrize("name", ["tiny-qwen3", "tiny-smol-q4"])
+def test_cli_info_and_tokenize_on_the_dropin_library(cli, name):
+    model = synth.ensure_model(name)
+    ref = ref_cli()
+    assert run_cli(cli, "info", model) == run_cli(ref, "info", model)
+    text = "Once upon a time, 42 foxes"
+    got = run_cli(cli, "tokenize", model, text)
+    assert got == run_cli(ref, "tokenize", model, text) and got[0] == 0 and got[1].strip()
+
+
+@pytest.mark.parametrize("target", ["q8_0", "q4_0"])
+def test_cli_quantize_on_the_dropin_library(cli, tmp_path, target):
+    """`ember quantize` runs this library's ember_quantize_file; the file equals the
+    reference CLI's byte for byte"""
+    src = str(tmp_path / "f32.ember")
+    synth.write_model(src, synth.CONFIGS["tiny-qwen2"], seed=5, quant="f32")
+    ours, refs = str(tmp_path / "ours.ember"), str(tmp_path / "ref.ember")
+    assert run_cli(cli, "quantize", src, ours, target)[0] == 0
+    assert run_cli(ref_cli(), "quantize", src, refs, target)[0] == 0
+    assert open(ours, "rb").read() == open(refs, "rb").read()
