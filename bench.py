@@ -178,31 +178,64 @@ def ref_cli_bench(binary, model, pp, tg, threads, reps=1):
 
 
 def thread_sweep():
+    """1, 2, 4, 8, ... up to the host's core count, and the count itself"""
     n = os.cpu_count() or 1
-    return sorted(c for c in {1, 4, 8, n // 2, n} if 1 <= c <= n)
+    ts, t = [], 1
+    while t < n:
+        ts.append(t)
+        t *= 2
+    return ts + [n]
 
 
-def cpu_baseline(model, depth, budget_tg=16):
-    """reference `ember bench` at depth `depth`, best decode over a thread sweep"""
+def reference_model(name, binary):
+    """The reference arm's own copy of the synthetic model: the fp32 file from
+    the numpy writer (no native library involved), quantized by the reference's
+    CLI (`ember quantize`, its own quantizer). Its tensors are byte-identical to
+    the file this library's arm loads (tests/test_quant_file.py)."""
+    from emberllm_b200 import synth      # pure Python: loads no shared library
+    cfg = synth.CONFIGS[name]
+    d = synth.cache_dir()
+    f32 = synth.ensure_model(name, quant="f32", directory=d)
+    out = os.path.join(d, os.path.basename(f32).replace("-f32-", "-refq-%s-" % cfg["quant"]))
+    if not os.path.exists(out):
+        tmp = out + ".tmp%d" % os.getpid()
+        r = subprocess.run([binary, "quantize", f32, tmp, cfg["quant"]], capture_output=True, text=True,
+                           timeout=1800)
+        if r.returncode != 0:
+            raise RuntimeError("reference quantize failed: " + r.stderr[-300:])
+        os.replace(tmp, out)
+    return out
+
+
+def sweep_threads(binary, model, depth, tg=16):
+    """decode tok/s of the reference at each thread count (short runs)"""
+    sweep = {}
+    for t in thread_sweep():
+        try:
+            sweep[t] = round(ref_cli_bench(binary, model, depth, tg, t)[0], 1)
+        except (RuntimeError, subprocess.TimeoutExpired):
+            pass
+    return sweep
+
+
+def cpu_baseline(depth, ntok, model_name):
+    """the reference's `ember bench` on the host cores: best thread count of a
+    sweep, then one run of the bench workload (pp depth, tg ntok) at that count"""
     binary = reference_binary()
     if not binary:
         return None
-    best = (0.0, 1, None)
-    for t in thread_sweep():
-        try:
-            tg, pp = ref_cli_bench(binary, model, depth, budget_tg, t)
-        except (RuntimeError, subprocess.TimeoutExpired):
-            continue
-        if tg > best[0]:
-            best = (tg, t, pp)
-    if best[0] == 0.0:
+    model = reference_model(model_name, binary)
+    sweep = sweep_threads(binary, model, depth)
+    if not sweep:
         return None
-    return {"value": round(best[0], 2), "unit": "tok/s", "cores": best[1], "kind": "reference",
-            "prefill_tok_s": best[2],
-            "sample": "reference `ember bench --pp %d --tg %d --reps 1` (%s, shipped -O3 "
-                      "-ffast-math flags), decode tok/s at depth %d, best of threads %s on %d "
-                      "host cores" % (depth, budget_tg, os.path.basename(binary), depth,
-                                      thread_sweep(), os.cpu_count() or 1)}
+    best = max(sweep, key=sweep.get)
+    tg, pp = ref_cli_bench(binary, model, depth, ntok, best)
+    return {"value": round(tg, 2), "unit": "tok/s", "cores": best, "kind": "reference",
+            "prefill_tok_s": pp,
+            "sample": "reference `ember bench --pp %d --tg %d --reps 1` (%s, shipped -O3 -ffast-math "
+                      "flags) on its own quantization of the same synthetic model, %d threads, the "
+                      "best of a sweep %s (tok/s by thread count, --tg 16) on %d host cores"
+                      % (depth, ntok, os.path.basename(binary), best, sweep, os.cpu_count() or 1)}
 
 
 # ------------------------------------------------------------------ ranks -----
@@ -479,11 +512,7 @@ def run_ours(args, world, rank, local, dist):
         "vs_baseline": None,
         "dtype": "int8 dot / fp32 (Q8_0 weights, exact reference arithmetic)",
         "data": "synthetic: N(0,0.02) weights seed 0, uniform random prompt seed 1",
-        "config": {"workload": "%s Q8_0 single-stream greedy decode of %d tokens at depth %d"
-                               % (args.config, ntok, depth),
-                   "model": args.config, "depth": depth, "tokens_per_step": ntok,
-                   "kv_cache": "fp16" if args.kv_fp16 else "fp32", "parallelism": "replicas, one per GPU" if world > 1 else "1 GPU",
-                   "l2": "weights 634 MB per token > 126 MB L2 (no flush needed)"},
+        "config": _workload_config(args, world),
         "hbm_gbs_step": round((step_bytes + kv_bytes) * value / world / 1e9, 1),
         "bytes_per_token": int(step_bytes + kv_bytes),
         "prefill_tok_s": round(world * npf / prefill_s, 1),
@@ -502,47 +531,64 @@ def run_ours(args, world, rank, local, dist):
         "clocks": clk,
     }
     if rank == 0 and world == 1 and args.cpu_baseline:
-        cb = cpu_baseline(path, depth)
-        line["cpu_baseline"] = cb
+        line["cpu_baseline"] = cpu_baseline(depth, ntok, args.config)
     return line
 
 
 def run_reference(args, world, rank):
-    """the reference's own CPU implementation on this host (oracle/_ref)"""
+    """The reference's own CPU implementation on this host: its CLI (oracle/_ref,
+    built from its sources with its shipped flags) running `ember bench` on its
+    own quantization of the synthetic model -- no library of this repository is
+    loaded. Same workload as this library's arm: prefill `--depth` tokens, then
+    `--tokens` decode steps; the thread count is the best of a sweep."""
     if rank != 0:
         return None
-    from emberllm_b200 import synth
     binary = reference_binary()
     if not binary:
         return {"impl": "reference", "unavailable": "oracle/_ref was not built on this machine"}
-    path = synth.ensure_model(args.config)
-    depth, tg = args.depth, 16
-    sweep = {}
-    for t in thread_sweep():
-        try:
-            sweep[t] = ref_cli_bench(binary, path, depth, tg, t)[0]
-        except (RuntimeError, subprocess.TimeoutExpired):
-            pass
+    model = reference_model(args.config, binary)
+    depth, ntok = args.depth, args.tokens
+    sweep = sweep_threads(binary, model, depth)
     best_t = max(sweep, key=sweep.get)
     for _ in range(max(0, args.warmup - 1)):
-        ref_cli_bench(binary, path, depth, tg, best_t)
-    vals = [ref_cli_bench(binary, path, depth, tg, best_t)[0] for _ in range(args.steps)]
-    v = statistics.mean(vals)
+        ref_cli_bench(binary, model, depth, ntok, best_t)
+    steps = [ref_cli_bench(binary, model, depth, ntok, best_t) for _ in range(args.steps)]
+    v = statistics.mean(tg for tg, _ in steps)
+    pp512 = None
+    try:
+        pp512 = round(ref_cli_bench(binary, model, args.prefill_tokens, 1, best_t)[1], 1)
+    except (RuntimeError, subprocess.TimeoutExpired):
+        pass
     return {
         "impl": "reference",
         "metric": "decode tok/s (Qwen3-0.6B Q8_0, 1 GPU); HBM GB/s; prefill tok/s",
         "value": round(v, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(tg / v * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot / fp32 (Q8_0)",
-        "data": "synthetic: N(0,0.02) weights seed 0",
-        "config": {"workload": "%s Q8_0 decode at depth %d (reference CPU, %d tokens per step)"
-                               % (args.config, depth, tg), "model": args.config},
+        "warmup": args.warmup, "ms_per_step": round(ntok / v * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 dot / fp32 (Q8_0 weights, exact reference arithmetic)",
+        "data": "synthetic: N(0,0.02) weights seed 0; token ids from the reference bench's own "
+                "fixed stream (decode time does not depend on the ids)",
+        "config": _workload_config(args, world),
+        "prefill_tok_s": pp512,
+        "prefill_note": "reference `ember bench --pp %d --tg 1` at %d threads" % (args.prefill_tokens, best_t),
         "cpu_baseline": {"value": round(v, 2), "unit": "tok/s", "cores": best_t, "kind": "reference",
-                         "sample": "reference `ember bench --pp %d --tg %d --reps 1` per step, "
-                                   "%s, threads %d (best of %s)"
-                                   % (depth, tg, os.path.basename(binary), best_t, sweep)},
+                         "sample": "reference `ember bench --pp %d --tg %d --reps 1` per step (%s, shipped "
+                                   "-O3 -ffast-math flags) on its own quantization of the synthetic model, "
+                                   "%d threads: the best of the sweep %s (tok/s by thread count, --tg 16) "
+                                   "on %d host cores" % (depth, ntok, os.path.basename(binary), best_t,
+                                                         sweep, os.cpu_count() or 1)},
         "e2e": {"value": round(v, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+
+
+def _workload_config(args, world):
+    """the `config` object both arms report for the single-stream workload"""
+    return {"workload": "%s Q8_0 single-stream greedy decode of %d tokens at depth %d"
+                        % (args.config, args.tokens, args.depth),
+            "model": args.config, "depth": args.depth, "tokens_per_step": args.tokens,
+            "kv_cache": "fp16" if args.kv_fp16 else "fp32",
+            "parallelism": "replicas, one per GPU" if world > 1 else "1 GPU",
+            "l2": "weights 634 MB per token > 126 MB L2 (no flush needed)"}
 
 
 def main():

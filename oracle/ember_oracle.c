@@ -4,10 +4,11 @@
  * Each function states the reference lines it follows. What matters for parity
  * is the order of every fp32 operation that feeds an int8 quantization, the KV
  * cache or the logits; those orders are spelled out in the comments. Build with
- * the reference's deterministic flags (-O2 -fno-fast-math -ffp-contract=off) so
- * the compiler neither fuses multiply-adds nor reorders sums. Rows of a matmul
- * and heads of attention are independent, so splitting them over threads does
- * not change any result.
+ * -fno-fast-math -ffp-contract=off (oracle/Makefile; -O3, which vectorizes only
+ * independent lanes and integer sums without -ffast-math) so the compiler neither
+ * fuses multiply-adds nor reorders a floating-point sum. Rows of a matmul, heads
+ * of attention and the tokens of a prefill chunk are independent, so splitting
+ * them over threads does not change any result.
  *
  * Parity pin: see ember_oracle.h.
  */
@@ -213,17 +214,14 @@ void orc_matmul(float *out, const float *x, const void *w, int dtype, int n_in, 
     rows_matmul(out, xin, w, dtype, n_in, d_out);
 }
 
-/* ref src/kernels.c:250-264: per token the same arithmetic as orc_matmul */
+/* ref src/kernels.c:250-264: per token the same arithmetic as orc_matmul
+ * (batch_matmul below: every column quantized into xq, one dot per row and
+ * column) */
+static void batch_matmul(float *out, const float *x, const void *w, int dtype, int n_in, int d_out, int n, Q8 *xq);
+
 void orc_matmul_batch(float *out, const float *x, const void *w, int dtype, int n_in,
                       int d_out, int B, void *xq) {
-    int nb = n_in / QB;
-    float *col = malloc(sizeof(float) * (size_t)d_out);
-    for (int b = 0; b < B; b++) {
-        void *xqb = dtype != DT_F32 ? (void *)((Q8 *)xq + (size_t)b * nb) : NULL;
-        orc_matmul(col, x + (size_t)b * n_in, w, dtype, n_in, d_out, xqb);
-        for (int r = 0; r < d_out; r++) out[(size_t)b * d_out + r] = col[r];
-    }
-    free(col);
+    batch_matmul(out, x, w, dtype, n_in, d_out, B, (Q8 *)xq);
 }
 
 /* ---- model pieces (ref src/model.c:50-100) --------------------------------- */
@@ -364,38 +362,67 @@ void orc_state_free(OrcState *s) {
 
 int orc_state_ctx(const OrcState *s) { return s->ctx; }
 
-static float kv_get(const OrcState *s, const void *base, size_t i) {
-    return s->f16kv ? orc_f16_to_f32(((const uint16_t *)base)[i]) : ((const float *)base)[i];
+
+/* fp16 -> fp32 of every half value, filled once (the widening is exact) */
+static float g_f16[65536];
+static pthread_once_t g_f16_once = PTHREAD_ONCE_INIT;
+static void f16_table_init(void) {
+    for (uint32_t i = 0; i < 65536u; i++) g_f16[i] = orc_f16_to_f32((uint16_t)i);
 }
 
-/* one query position over the cache, per head (ref src/model.c:221-259) */
+/* row of hd cached values at element offset `base`, widened to fp32 */
+static const float *kv_row(const OrcState *s, const void *cache, size_t base, int hd, float *buf) {
+    if (!s->f16kv) return (const float *)cache + base;
+    const uint16_t *h = (const uint16_t *)cache + base;
+    for (int i = 0; i < hd; i++) buf[i] = g_f16[h[i]];
+    return buf;
+}
+
+/* One query position over the cache for one head (ref src/model.c:221-259):
+ * scores sc_t = sum_i q_i*k_t,i in index order, then * inv_sqrt; softmax; then
+ * out_i = sum_t w_t*v_t,i in position order. The score chains of different
+ * positions are independent, so eight of them advance side by side here (keys
+ * staged dimension-major); each one still adds its products in index order.
+ * `att` is scratch of pos+1 floats; hd <= 256. */
+static void attend_one(const OrcState *s, int l, int pos, const float *qh, int h, float *att, float *out) {
+    int hd = s->hd, kvd = s->kvd, mul = s->nh / s->nkv, kvh = h / mul;
+    size_t lo = (size_t)l * s->ctx * kvd;
+    float inv_sqrt = 1.0f / sqrtf((float)hd);
+    float tile[256][8], buf[256];
+    pthread_once(&g_f16_once, f16_table_init);
+    int t = 0;
+    for (; t + 8 <= pos + 1; t += 8) {
+        for (int j = 0; j < 8; j++) {
+            const float *kr = kv_row(s, s->kc, lo + (size_t)(t + j) * kvd + (size_t)kvh * hd, hd, buf);
+            for (int i = 0; i < hd; i++) tile[i][j] = kr[i];
+        }
+        float sc[8] = { 0, 0, 0, 0, 0, 0, 0, 0 };
+        for (int i = 0; i < hd; i++)
+            for (int j = 0; j < 8; j++) sc[j] += qh[i] * tile[i][j];
+        for (int j = 0; j < 8; j++) att[t + j] = sc[j] * inv_sqrt;
+    }
+    for (; t <= pos; t++) {
+        const float *kr = kv_row(s, s->kc, lo + (size_t)t * kvd + (size_t)kvh * hd, hd, buf);
+        float sc = 0.0f;
+        for (int i = 0; i < hd; i++) sc += qh[i] * kr[i];
+        att[t] = sc * inv_sqrt;
+    }
+    softmax(att, pos + 1);
+    for (int i = 0; i < hd; i++) out[i] = 0.0f;
+    for (t = 0; t <= pos; t++) {
+        float w = att[t];
+        const float *vr = kv_row(s, s->vc, lo + (size_t)t * kvd + (size_t)kvh * hd, hd, buf);
+        for (int i = 0; i < hd; i++) out[i] += w * vr[i];
+    }
+}
+
 typedef struct { OrcState *s; int l, pos; } AT;
 
 static void attend_heads(void *c, int h0, int h1) {
     const AT *a = c;
     OrcState *s = a->s;
-    int l = a->l, pos = a->pos;
-    int hd = s->hd, kvd = s->kvd, mul = s->nh / s->nkv;
-    size_t lo = (size_t)l * s->ctx * kvd;
-    float inv_sqrt = 1.0f / sqrtf((float)hd);
-    for (int h = h0; h < h1; h++) {
-        const float *qh = s->q + h * hd;
-        float *att = s->att + (size_t)h * s->ctx, *out = s->xb + h * hd;
-        int kvh = h / mul;
-        for (int i = 0; i < hd; i++) out[i] = 0.0f;
-        for (int t = 0; t <= pos; t++) {
-            float sc = 0.0f;
-            size_t base = lo + (size_t)t * kvd + (size_t)kvh * hd;
-            for (int i = 0; i < hd; i++) sc += qh[i] * kv_get(s, s->kc, base + i);
-            att[t] = sc * inv_sqrt;
-        }
-        softmax(att, pos + 1);
-        for (int t = 0; t <= pos; t++) {
-            float w = att[t];
-            size_t base = lo + (size_t)t * kvd + (size_t)kvh * hd;
-            for (int i = 0; i < hd; i++) out[i] += w * kv_get(s, s->vc, base + i);
-        }
-    }
+    for (int h = h0; h < h1; h++)
+        attend_one(s, a->l, a->pos, s->q + h * s->hd, h, s->att + (size_t)h * s->ctx, s->xb + h * s->hd);
 }
 
 static void attend(OrcState *s, int l, int pos) {
@@ -458,15 +485,224 @@ float *orc_forward(OrcState *s, int tok, int pos) {
     return s->logits;
 }
 
-/* ref src/model.c:283-360 batches the matmuls over tokens, but every token's
- * arithmetic is the one orc_forward performs (same per-row dots, same per-token
- * norms/rope/attention, attention of token b reading only positions <= start+b);
- * the reference's prefill is therefore bit-identical to sequential forwards,
- * which is what this restatement does. lm_head runs for every token here, which
- * leaves the last token's logits unchanged. */
+/* ---- batched prefill (ref src/model.c:283-360) ------------------------------
+ * The reference's prefill runs every layer over all n tokens at once: each
+ * matmul quantizes every token's activation and streams each weight row once for
+ * all tokens (ember_matmul_batch, ref src/kernels.c:227-264, the same per-(row,
+ * token) dot as ember_matmul); norms, bias, QK-norm, RoPE and the KV store run
+ * per token; then attention per token, token b reading positions <= start+b;
+ * only the last token's logits are computed. Every token's arithmetic is the one
+ * orc_forward performs. Tokens go through in chunks of PF_CHUNK, which changes
+ * nothing: a chunk's attention reads only positions written before it or by its
+ * own KV store. */
+enum { PF_CHUNK = 256 };
+
+typedef struct { float *out; const Q8 *xq; const void *w; int dtype, n_in, d_out, n; const float *xf; } BMM;
+
+/* int8 dot of one block pair: exact in any order */
+static int32_t block_dot_q8(const int8_t *w, const int8_t *x) {
+    int32_t acc = 0;
+    for (int i = 0; i < QB; i++) acc += (int32_t)w[i] * (int32_t)x[i];
+    return acc;
+}
+
+static int32_t block_dot_q4(const uint8_t *w, const int8_t *x) {
+    int32_t acc = 0;
+    for (int i = 0; i < QB / 2; i++)
+        acc += ((int32_t)(w[i] & 15) - 8) * x[i] + ((int32_t)(w[i] >> 4) - 8) * x[i + QB / 2];
+    return acc;
+}
+
+/* Per (row, token): the chain of dot_q8 / dot_q4, sum over blocks in block order
+ * of ((float)acc * d_w) * d_x, with the fp16 scales widened once per row and per
+ * token (the widening is exact, so this changes no result). */
+static void bmm_slice(void *c, int r0, int r1) {
+    const BMM *a = c;
+    int nb = a->n_in / QB;
+    float *dw = malloc(sizeof(float) * (size_t)(nb + 1));
+    float *dx = malloc(sizeof(float) * (size_t)a->n * (nb + 1));
+    if (!dw || !dx) fatal("out of memory");
+    if (a->dtype != DT_F32)
+        for (int b = 0; b < a->n; b++)
+            for (int k = 0; k < nb; k++) dx[(size_t)b * nb + k] = orc_f16_to_f32(a->xq[(size_t)b * nb + k].d);
+    for (int r = r0; r < r1; r++) {
+        if (a->dtype == DT_F32) {
+            for (int b = 0; b < a->n; b++)
+                a->out[(size_t)b * a->d_out + r] =
+                    dot_f32((const float *)a->w + (size_t)r * a->n_in, a->xf + (size_t)b * a->n_in, a->n_in);
+            continue;
+        }
+        const Q8 *w8 = (const Q8 *)a->w + (size_t)r * nb;
+        const Q4 *w4 = (const Q4 *)a->w + (size_t)r * nb;
+        for (int k = 0; k < nb; k++) dw[k] = orc_f16_to_f32(a->dtype == DT_Q8 ? w8[k].d : w4[k].d);
+        for (int b = 0; b < a->n; b++) {
+            const Q8 *xb = a->xq + (size_t)b * nb;
+            const float *dxb = dx + (size_t)b * nb;
+            float s = 0.0f;
+            for (int k = 0; k < nb; k++) {
+                int32_t acc = a->dtype == DT_Q8 ? block_dot_q8(w8[k].qs, xb[k].qs) : block_dot_q4(w4[k].qs, xb[k].qs);
+                s += (float)acc * dw[k] * dxb[k];
+            }
+            a->out[(size_t)b * a->d_out + r] = s;
+        }
+    }
+    free(dw);
+    free(dx);
+}
+
+/* out[b][d_out] = W x[b] for b < n; xq: n * (n_in/32) Q8 blocks of scratch */
+static void batch_matmul(float *out, const float *x, const void *w, int dtype, int n_in, int d_out, int n, Q8 *xq) {
+    int nb = n_in / QB;
+    if (dtype != DT_F32)
+        for (int b = 0; b < n; b++) orc_quantize_q8_0(x + (size_t)b * n_in, xq + (size_t)b * nb, n_in);
+    BMM a = { out, xq, w, dtype, n_in, d_out, n, x };
+    par_for(bmm_slice, &a, d_out, 1);
+}
+
+/* Attention of a chunk of n query tokens (positions start..start+n-1), one head
+ * per work item: the same per-(token, head) arithmetic as attend_one -- every
+ * score chain over the dimensions in index order, softmax, every output chain
+ * over the positions in order -- with the loops arranged so that each staged key
+ * tile and each value row serves all tokens that attend to it. */
+typedef struct { OrcState *s; int l, start, n; const float *Q; float *O; } BAT;
+
+static void battend_head(void *c, int h0, int h1) {
+    const BAT *a = c;
+    OrcState *s = a->s;
+    int hd = s->hd, kvd = s->kvd, mul = s->nh / s->nkv, qd = s->nh * hd, n = a->n, start = a->start;
+    int T = start + n;                       /* positions the last token attends: 0..T-1 */
+    size_t lo = (size_t)a->l * s->ctx * kvd;
+    float inv_sqrt = 1.0f / sqrtf((float)hd);
+    float *att = malloc(sizeof(float) * (size_t)n * T);
+    if (!att) fatal("out of memory");
+    float tile[256][8], buf[256];
+    pthread_once(&g_f16_once, f16_table_init);
+    for (int h = h0; h < h1; h++) {
+        int kvh = h / mul;
+        /* scores: token b attends positions 0..start+b */
+        int t = 0;
+        for (; t + 8 <= T; t += 8) {
+            for (int j = 0; j < 8; j++) {
+                const float *kr = kv_row(s, s->kc, lo + (size_t)(t + j) * kvd + (size_t)kvh * hd, hd, buf);
+                for (int i = 0; i < hd; i++) tile[i][j] = kr[i];
+            }
+            int b0 = t + 7 - start;          /* first token that sees all 8 positions */
+            if (b0 < 0) b0 = 0;
+            for (int b = b0; b < n; b++) {
+                const float *qh = a->Q + (size_t)b * qd + h * hd;
+                float sc[8] = { 0, 0, 0, 0, 0, 0, 0, 0 };
+                for (int i = 0; i < hd; i++)
+                    for (int j = 0; j < 8; j++) sc[j] += qh[i] * tile[i][j];
+                for (int j = 0; j < 8; j++) att[(size_t)b * T + t + j] = sc[j] * inv_sqrt;
+            }
+            for (int b = 0; b < b0 && b < n; b++)      /* tokens that see only part of the tile */
+                for (int j = 0; j < 8 && t + j <= start + b; j++) {
+                    const float *qh = a->Q + (size_t)b * qd + h * hd;
+                    float sc = 0.0f;
+                    for (int i = 0; i < hd; i++) sc += qh[i] * tile[i][j];
+                    att[(size_t)b * T + t + j] = sc * inv_sqrt;
+                }
+        }
+        for (; t < T; t++) {
+            const float *kr = kv_row(s, s->kc, lo + (size_t)t * kvd + (size_t)kvh * hd, hd, buf);
+            for (int b = t - start < 0 ? 0 : t - start; b < n; b++) {
+                const float *qh = a->Q + (size_t)b * qd + h * hd;
+                float sc = 0.0f;
+                for (int i = 0; i < hd; i++) sc += qh[i] * kr[i];
+                att[(size_t)b * T + t] = sc * inv_sqrt;
+            }
+        }
+        for (int b = 0; b < n; b++) {
+            softmax(att + (size_t)b * T, start + b + 1);
+            float *out = a->O + (size_t)b * qd + h * hd;
+            for (int i = 0; i < hd; i++) out[i] = 0.0f;
+        }
+        /* outputs: out_b,i += w_b,t * v_t,i for t in order */
+        for (t = 0; t < T; t++) {
+            const float *vr = kv_row(s, s->vc, lo + (size_t)t * kvd + (size_t)kvh * hd, hd, buf);
+            for (int b = t - start < 0 ? 0 : t - start; b < n; b++) {
+                float w = att[(size_t)b * T + t];
+                float *out = a->O + (size_t)b * qd + h * hd;
+                for (int i = 0; i < hd; i++) out[i] += w * vr[i];
+            }
+        }
+    }
+    free(att);
+}
+
+static void prefill_chunk(OrcState *s, const int *ids, int n, int start, float *X, float *Xn, float *Tmp,
+                          float *Q, float *K, float *V, float *O, float *H1, float *H2, Q8 *xq) {
+    int dim = s->dim, hd = s->hd, nh = s->nh, kvd = s->kvd, qd = nh * hd, hid = s->hidden;
+    for (int b = 0; b < n; b++) embed(s, ids[b], X + (size_t)b * dim);
+    for (int l = 0; l < s->L; l++) {
+        for (int b = 0; b < n; b++) orc_rmsnorm(Xn + (size_t)b * dim, X + (size_t)b * dim, s->an[l], dim, s->eps);
+        batch_matmul(Q, Xn, s->wq[l].p, s->wq[l].dt, dim, qd, n, xq);
+        batch_matmul(K, Xn, s->wk[l].p, s->wk[l].dt, dim, kvd, n, xq);
+        batch_matmul(V, Xn, s->wv[l].p, s->wv[l].dt, dim, kvd, n, xq);
+        for (int b = 0; b < n; b++) {
+            float *qb = Q + (size_t)b * qd, *kb = K + (size_t)b * kvd, *vb = V + (size_t)b * kvd;
+            int pos = start + b;
+            if (s->bq[l]) for (int i = 0; i < qd; i++) qb[i] += s->bq[l][i];
+            if (s->bk[l]) for (int i = 0; i < kvd; i++) kb[i] += s->bk[l][i];
+            if (s->bv[l]) for (int i = 0; i < kvd; i++) vb[i] += s->bv[l][i];
+            if (s->qkn && s->qn[l]) {
+                for (int h = 0; h < nh; h++) orc_rmsnorm(qb + h * hd, qb + h * hd, s->qn[l], hd, s->eps);
+                for (int h = 0; h < s->nkv; h++) orc_rmsnorm(kb + h * hd, kb + h * hd, s->kn[l], hd, s->eps);
+            }
+            rope(qb, qd, hd, pos, s->theta, s->neox);
+            rope(kb, kvd, hd, pos, s->theta, s->neox);
+            size_t off = ((size_t)l * s->ctx + pos) * kvd;
+            for (int i = 0; i < kvd; i++) {
+                if (s->f16kv) {
+                    ((uint16_t *)s->kc)[off + i] = orc_f32_to_f16(kb[i]);
+                    ((uint16_t *)s->vc)[off + i] = orc_f32_to_f16(vb[i]);
+                } else {
+                    ((float *)s->kc)[off + i] = kb[i];
+                    ((float *)s->vc)[off + i] = vb[i];
+                }
+            }
+        }
+        BAT at = { s, l, start, n, Q, O };
+        par_for(battend_head, &at, nh, 1);
+        batch_matmul(Tmp, O, s->wo[l].p, s->wo[l].dt, qd, dim, n, xq);
+        for (size_t i = 0; i < (size_t)n * dim; i++) X[i] += Tmp[i];
+        for (int b = 0; b < n; b++) orc_rmsnorm(Xn + (size_t)b * dim, X + (size_t)b * dim, s->fn[l], dim, s->eps);
+        batch_matmul(H1, Xn, s->w1[l].p, s->w1[l].dt, dim, hid, n, xq);
+        batch_matmul(H2, Xn, s->w3[l].p, s->w3[l].dt, dim, hid, n, xq);
+        for (size_t i = 0; i < (size_t)n * hid; i++) {
+            float g = H1[i];
+            H1[i] = g / (1.0f + expf(-g)) * H2[i];
+        }
+        batch_matmul(Tmp, H1, s->w2[l].p, s->w2[l].dt, hid, dim, n, xq);
+        for (size_t i = 0; i < (size_t)n * dim; i++) X[i] += Tmp[i];
+    }
+}
+
 float *orc_prefill(OrcState *s, const int *ids, int n, int start) {
     if (n <= 0) return s->logits;
-    for (int b = 0; b < n; b++) orc_forward(s, ids[b], start + b);
+    if (start < 0 || start + n > s->ctx) fatal("prefill past the context");
+    for (int b = 0; b < n; b++)
+        if (ids[b] < 0 || ids[b] >= s->vocab) fatal("token id out of range");
+    int c = n < PF_CHUNK ? n : PF_CHUNK;
+    int dim = s->dim, qd = s->nh * s->hd, wide = dim;
+    if (s->hidden > wide) wide = s->hidden;
+    if (qd > wide) wide = qd;
+    float *X = malloc(sizeof(float) * (size_t)c * dim), *Xn = malloc(sizeof(float) * (size_t)c * dim);
+    float *Tmp = malloc(sizeof(float) * (size_t)c * dim), *Q = malloc(sizeof(float) * (size_t)c * qd);
+    float *K = malloc(sizeof(float) * (size_t)c * s->kvd), *V = malloc(sizeof(float) * (size_t)c * s->kvd);
+    float *O = malloc(sizeof(float) * (size_t)c * qd), *H1 = malloc(sizeof(float) * (size_t)c * s->hidden);
+    float *H2 = malloc(sizeof(float) * (size_t)c * s->hidden);
+    Q8 *xq = malloc(sizeof(Q8) * (size_t)c * (wide / QB + 1));
+    if (!X || !Xn || !Tmp || !Q || !K || !V || !O || !H1 || !H2 || !xq) fatal("out of memory");
+    int last = 0;
+    for (int b0 = 0; b0 < n; b0 += c) {
+        int m = n - b0 < c ? n - b0 : c;
+        prefill_chunk(s, ids + b0, m, start + b0, X, Xn, Tmp, Q, K, V, O, H1, H2, xq);
+        last = m - 1;
+    }
+    orc_rmsnorm(s->x, X + (size_t)last * dim, s->fnorm, dim, s->eps);
+    orc_matmul(s->logits, s->x, s->head.p, s->head.dt, dim, s->vocab, s->xq);
+    free(X); free(Xn); free(Tmp); free(Q); free(K); free(V); free(O); free(H1); free(H2); free(xq);
     return s->logits;
 }
 

@@ -100,3 +100,54 @@ def test_oracle_stories110m_first_steps_match_reference(orc):
     assert np.array_equal(H.bits(a.prefill(ids)), H.bits(b.prefill(ids)))
     a.close()
     b.close()
+
+
+@pytest.mark.skipif(not H.have_reference(), reason="reference build (oracle/_ref) not present")
+def test_oracle_long_prefill_chunks_match_reference(orc):
+    """a 600-token prompt: the oracle's batched prefill goes through it in chunks
+    of 256 tokens, the reference's in one batch; logits and the following steps
+    agree bit for bit"""
+    ref = H.ApiLib(H.REF_DET)
+    path = synth.ensure_model("tiny-long")
+    a, b = ref.session(path, 700, 0), orc.session(path, 700, 0)
+    rng = np.random.default_rng(11)
+    ids = rng.integers(0, a.vocab, 600)
+    assert np.array_equal(H.bits(a.prefill(ids)), H.bits(b.prefill(ids)))
+    for pos in range(600, 604):
+        t = int(rng.integers(0, a.vocab))
+        assert np.array_equal(H.bits(a.forward(t, pos)), H.bits(b.forward(t, pos)))
+    a.close()
+    b.close()
+
+
+_REF_THREADS = []
+
+
+def _ref_threads(ref):
+    """start the reference's thread pool once per process (its rows split over
+    threads give the same results; a second ember_threads_init would restart
+    the pool under the running workers)"""
+    if not _REF_THREADS:
+        ref.lib.ember_threads_init(min(16, os.cpu_count() or 1))
+        _REF_THREADS.append(1)
+
+
+@pytest.mark.skipif(not H.have_reference(), reason="reference build (oracle/_ref) not present")
+@pytest.mark.parametrize("name", ["qwen3-0.6b", "qwen2.5-0.5b", "smollm2-135m"])
+def test_oracle_fullsize_qwen_steps_match_reference(orc, name):
+    """the full-size BASELINE shapes -- head_dim 128 with QK-norm (Qwen3), q/k/v
+    biases (Qwen2.5), Q4_0 layers (SmolLM2), a 151,936 or 49,152-entry vocab --
+    through the reference and the oracle: a 20-token prefill, then teacher-forced
+    steps, logits bit for bit"""
+    ref = H.ApiLib(H.REF_DET)
+    _ref_threads(ref)
+    path = synth.ensure_model(name)
+    a, b = ref.session(path, 64, 0), orc.session(path, 64, 0)
+    rng = np.random.default_rng(21)
+    ids = rng.integers(0, a.vocab, 20)
+    assert np.array_equal(H.bits(a.prefill(ids)), H.bits(b.prefill(ids)))
+    for pos in range(20, 23):
+        t = int(rng.integers(0, a.vocab))
+        assert np.array_equal(H.bits(a.forward(t, pos)), H.bits(b.forward(t, pos)))
+    a.close()
+    b.close()
