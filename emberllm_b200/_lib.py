@@ -62,7 +62,7 @@ CUDA_SYMBOLS = [
     "ember_cuda_state_logits_dev", "ember_cuda_state_launches_per_step", "ember_cuda_error",
     "ember_cuda_available", "ember_cuda_profile_step", "ember_cuda_mark", "ember_cuda_elapsed_ms",
     "ember_cuda_time_kernel", "ember_cuda_argmax_static", "ember_host_expf_params",
-    "ember_host_expf_emulated", "ember_cuda_split_sum_batch",
+    "ember_host_expf_emulated",
     "ember_host_rope_table", "ember_forward_greedy", "ember_state_cuda",
     "ember_cuda_batch_new", "ember_cuda_batch_free", "ember_cuda_batch_prefill", "ember_cuda_batch_greedy",
     "ember_cuda_batch_stream", "ember_batch_new", "ember_batch_free", "ember_batch_prefill",
@@ -139,7 +139,6 @@ def load(path=None):
     lib.ember_cuda_model_bytes.restype = ctypes.c_uint64
     lib.ember_cuda_model_bytes.argtypes = [_P]
     lib.ember_host_rope_table.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_float]
-    lib.ember_cuda_split_sum_batch.argtypes = [_P, ctypes.c_int, ctypes.c_int, _P, _P]
     _lib = lib
     return lib
 

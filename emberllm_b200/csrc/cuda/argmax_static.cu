@@ -21,7 +21,8 @@
 // Set-up. The first call on each device (the device that owns `logits`) looks up
 // the array's device address with cudaGetSymbolAddress while that device is
 // current, and caches it. Make that first call before any stream capture is
-// begun on the calling thread.
+// begun on the calling thread. The call selects that device to enqueue its work
+// and selects the caller's current device again before it returns.
 #include <cuda_runtime.h>
 
 #include <pthread.h>
@@ -48,7 +49,9 @@ __device__ __forceinline__ void take(float &bv, int &bi, float v, int i) {
 }
 
 // first index of the strict maximum of x[0..n) (the reference's greedy pick,
-// src/sample.c:114-118); NaN never wins; an all -inf/NaN input gives 0
+// src/sample.c:114-118: best = 0, then i wins when x[i] > x[best]). So a NaN
+// never wins, an all -inf/NaN input gives 0, and a NaN at index 0 gives 0 (no
+// value compares greater than it)
 __global__ void __launch_bounds__(kThreads) argmax_static_kernel(const float *x, int n, int *out,
                                                                  unsigned char *scratch) {
     float *part_v = reinterpret_cast<float *>(scratch);
@@ -102,7 +105,7 @@ __global__ void __launch_bounds__(kThreads) argmax_static_kernel(const float *x,
         __syncthreads();
     }
     if (threadIdx.x == 0) {
-        *out = si[0] == 0x7FFFFFFF ? 0 : si[0];
+        *out = (si[0] == 0x7FFFFFFF || isnan(x[0])) ? 0 : si[0];
         *ticket = 0u;
     }
 }
@@ -115,24 +118,29 @@ int report(int code, const char *what, const char *detail) {
     return code;
 }
 
-}  // namespace
-
-extern "C" int ember_cuda_argmax_static(const float *logits, int n, int *out_index, void *stream) {
-    if (n < 1 || (long long)n > kMaxN) {
-        char d[96];
-        snprintf(d, sizeof(d), "n = %d, allowed 1..%lld", n, kMaxN);
-        return report(kBadSize, "size outside the supported range", d);
-    }
-    if (!logits || !out_index) return report(kBadPointer, "null logits or output pointer", nullptr);
+// the device that owns device memory p, or -1 when p is not device memory
+int device_of(const void *p) {
     cudaPointerAttributes attr;
-    if (cudaPointerGetAttributes(&attr, logits) != cudaSuccess || attr.type != cudaMemoryTypeDevice) {
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
         cudaGetLastError();
-        return report(kBadPointer, "logits is not device memory", nullptr);
+        return -1;
     }
-    const int dev = attr.device;
-    if (dev < 0 || dev >= kMaxDevices) return report(kBadPointer, "device index too large", nullptr);
+    return attr.type == cudaMemoryTypeDevice ? attr.device : -1;
+}
+
+int argmax_static_on(int dev, const float *logits, int n, int *out_index, cudaStream_t st) {
     cudaError_t e = cudaSetDevice(dev);
     if (e != cudaSuccess) return report(kCudaError, "cannot select the logits' device", cudaGetErrorString(e));
+#if CUDART_VERSION >= 12080
+    if (st) {
+        int sdev = -1;
+        if (cudaStreamGetDevice(st, &sdev) != cudaSuccess) {
+            cudaGetLastError();
+            return report(kBadPointer, "stream is not a valid CUDA stream", nullptr);
+        }
+        if (sdev != dev) return report(kBadPointer, "stream belongs to another device than logits", nullptr);
+    }
+#endif
     // once per device, with that device current: the scratch array's device address
     pthread_mutex_lock(&g_mu);
     if (!g_scratch_addr[dev]) {
@@ -146,7 +154,6 @@ extern "C" int ember_cuda_argmax_static(const float *logits, int n, int *out_ind
     }
     unsigned char *scratch = (unsigned char *)g_scratch_addr[dev];
     pthread_mutex_unlock(&g_mu);
-    cudaStream_t st = (cudaStream_t)stream;
     const long long want = ((long long)n + kThreads * 4 - 1) / (kThreads * 4);
     const int grid = (int)(want < kMaxBlocks ? want : kMaxBlocks);
     // the completion ticket must start at zero: the array keeps the last call's contents
@@ -157,4 +164,28 @@ extern "C" int ember_cuda_argmax_static(const float *logits, int n, int *out_ind
     }
     if (e != cudaSuccess) return report(kCudaError, "launch failed", cudaGetErrorString(e));
     return kOk;
+}
+
+}  // namespace
+
+extern "C" int ember_cuda_argmax_static(const float *logits, int n, int *out_index, void *stream) {
+    if (n < 1 || (long long)n > kMaxN) {
+        char d[96];
+        snprintf(d, sizeof(d), "n = %d, allowed 1..%lld", n, kMaxN);
+        return report(kBadSize, "size outside the supported range", d);
+    }
+    if (!logits || !out_index) return report(kBadPointer, "null logits or output pointer", nullptr);
+    const int dev = device_of(logits);
+    if (dev < 0) return report(kBadPointer, "logits is not device memory", nullptr);
+    if (dev >= kMaxDevices) return report(kBadPointer, "device index too large", nullptr);
+    if (device_of(out_index) != dev) return report(kBadPointer, "out_index is not device memory of the logits' device", nullptr);
+    // the kernel runs on the logits' device; the caller's current device is put back
+    int prev = -1;
+    if (cudaGetDevice(&prev) != cudaSuccess) {
+        cudaGetLastError();
+        prev = -1;
+    }
+    const int rc = argmax_static_on(dev, logits, n, out_index, (cudaStream_t)stream);
+    if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+    return rc;
 }

@@ -91,7 +91,7 @@ __host__ __device__ inline size_t gemv_p_bytes(int cols, bool in_norm) {
     return pad16(p > pro ? p : pro);
 }
 
-// dynamic shared memory of gemv_kernel
+// dynamic shared memory of ember_q8_gemv_kernel
 __host__ inline size_t gemv_smem_bytes(const GemvArgs &a, bool need_xf, bool in_norm) {
     const int cols = a.cols, nb = cols / 32;
     size_t b = a.quantized ? (size_t)a.stages * a.stage_bytes : 0;
@@ -193,7 +193,7 @@ EMB_DEV void issue_tile(const GemvArgs &a, int t, unsigned char *dst, uint64_t *
 }
 
 template <int IN, int EPI>
-__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(GEMV_THREADS) ember_q8_gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[GEMV_MAX_STAGES];
     __shared__ double tab_s[EPI == EPI_SWIGLU ? 64 : 1];
@@ -692,7 +692,7 @@ struct ArgmaxArgs {
     int *out;
 };
 
-// first index of the strict maximum (ref src/sample.c:114-118)
+// first index of the strict maximum (ref src/sample.c:114-118); NaN never wins
 EMB_DEV void am_merge(float &bv, int &bi, float v, int i) {
     if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
 }
@@ -738,7 +738,9 @@ __global__ void __launch_bounds__(256) argmax_advance_kernel(const ArgmaxArgs a)
             int pi = *(volatile int *)&a.part_i[b];
             am_merge(v, idx, pv, pi);
         }
-        if (idx == 0x7FFFFFFF) idx = 0;   // all -inf/NaN: the reference keeps index 0
+        // all -inf/NaN, or a NaN at index 0 (nothing compares greater): the
+        // reference's loop keeps index 0
+        if (idx == 0x7FFFFFFF || isnan(a.logits[0])) idx = 0;
         a.ctl[CTL_TOK] = idx;
         a.ctl[CTL_POS] += 1;
         if (a.out) a.out[a.ctl[CTL_NOUT]] = idx;

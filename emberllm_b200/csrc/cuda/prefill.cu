@@ -583,7 +583,8 @@ __global__ void __launch_bounds__(256) batch_argmax_kernel(const float *logits, 
         __syncthreads();
     }
     if (tid == 0) {
-        const int idx = si[0] == 0x7FFFFFFF ? 0 : si[0];   // all NaN: the reference keeps index 0
+        // all -inf/NaN, or a NaN at index 0: the reference's loop keeps index 0
+        const int idx = (si[0] == 0x7FFFFFFF || isnan(row[0])) ? 0 : si[0];
         tok[s] = idx;
         pos[s] += 1;
         out[(size_t)(*nout) * S + s] = idx;
@@ -774,7 +775,12 @@ extern "C" int ember_cuda_batch_greedy(EmberCudaBatch *b, const int *toks, const
     if (!b->reps.empty()) {
         // every stream's steps enqueued before any wait, so that they run at once
         for (int i = 0; i < b->S; i++)
-            if (greedy_enqueue(b->reps[i], toks[i], pos[i], n_steps, b->htok + (size_t)i * b->max_steps)) return 1;
+            if (greedy_enqueue(b->reps[i], toks[i], pos[i], n_steps, b->htok + (size_t)i * b->max_steps)) {
+                // streams 0..i-1 still copy their tokens into the pinned buffer:
+                // wait for them before reporting the failure
+                for (int j = 0; j < i; j++) cudaStreamSynchronize(b->reps[j]->stream);
+                return 1;
+            }
         int rc = 0;
         for (int i = 0; i < b->S; i++) rc |= greedy_finish(b->reps[i]);
         if (rc) return 1;

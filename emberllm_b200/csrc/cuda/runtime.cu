@@ -89,8 +89,8 @@ static int init_kernel_attrs(int device) {
     if (device < 32 && ((done_mask >> device) & 1u)) return 0;
     int optin = 0;
     CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
-    if (allow_max_smem(gemv_kernel<IN_RAW, EPI_STORE>, optin) || allow_max_smem(gemv_kernel<IN_NORM, EPI_STORE>, optin) ||
-        allow_max_smem(gemv_kernel<IN_NORM, EPI_SWIGLU>, optin) || allow_max_smem(gemv_kernel<IN_QUANT, EPI_RESID>, optin) ||
+    if (allow_max_smem(ember_q8_gemv_kernel<IN_RAW, EPI_STORE>, optin) || allow_max_smem(ember_q8_gemv_kernel<IN_NORM, EPI_STORE>, optin) ||
+        allow_max_smem(ember_q8_gemv_kernel<IN_NORM, EPI_SWIGLU>, optin) || allow_max_smem(ember_q8_gemv_kernel<IN_QUANT, EPI_RESID>, optin) ||
         allow_max_smem(attn_decode_kernel<float>, optin) || allow_max_smem(attn_decode_kernel<__half>, optin) ||
         allow_max_smem(attn_scores_kernel<float, 1>, optin) || allow_max_smem(attn_scores_kernel<__half, 1>, optin) ||
         allow_max_smem(attn_scores_kernel<float, 2>, optin) || allow_max_smem(attn_scores_kernel<__half, 2>, optin) ||
@@ -439,7 +439,7 @@ static int run_gemv(GemvArgs a, int n_sm, cudaStream_t st, int *count, int max_c
         *smem_out = smem;
         int occ = 0;
         if (smem > 200 * 1024 ||
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_kernel<IN, EPI>, GEMV_THREADS, smem) != cudaSuccess)
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ember_q8_gemv_kernel<IN, EPI>, GEMV_THREADS, smem) != cudaSuccess)
             return 0;
         return occ;
     };
@@ -462,7 +462,7 @@ static int run_gemv(GemvArgs a, int n_sm, cudaStream_t st, int *count, int max_c
     if (grid < 1) grid = 1;
     resident(total <= grid ? 1 : best_stages, &smem);
     if (count) (*count)++;
-    CK(launch_pdl(gemv_kernel<IN, EPI>, grid, GEMV_THREADS, smem, st, a));
+    CK(launch_pdl(ember_q8_gemv_kernel<IN, EPI>, grid, GEMV_THREADS, smem, st, a));
     return 0;
 }
 

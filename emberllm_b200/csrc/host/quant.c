@@ -2,8 +2,8 @@
  * requantizer (replaces ref src/kernels.c:25-115 and src/quant.c:59-125).
  *
  * These run on the CPU because they produce the .ember file format offline;
- * the token loop's activation quantization is done on the GPU (see
- * csrc/cuda/exact.cuh). Every rounding step here follows the reference bit for
+ * the token loop's activation quantization is done on the GPU (quant_quad and
+ * quant_lane in csrc/cuda/common.cuh). Every rounding step here follows the reference bit for
  * bit, because the file bytes they produce are what both the reference and this
  * library then read: the tests compare ember_quantize_file's output byte for byte
  * against emberllm's `ember quantize`. Build with -ffp-contract=off.
@@ -117,7 +117,7 @@ static int stage_tensor(const EmberTensor *t, const void *src, int target, Stage
     int want = target;
     if (target == EMBER_DT_Q4_0 &&
         (strcmp(t->name, "tok_embeddings") == 0 || strcmp(t->name, "lm_head") == 0))
-        want = EMBER_DT_Q8_0;                      /* ref src/quant.c:167-171 */
+        want = EMBER_DT_Q8_0;                      /* ref src/quant.c:71-75 */
     int rows = t->shape[0], cols = t->shape[1];
     int quantize = t->dtype == EMBER_DT_F32 && t->ndim >= 2 && cols % EMBER_Q_BLOCK == 0 &&
                    want != EMBER_DT_F32;
@@ -163,7 +163,7 @@ static int write_zeros(FILE *f, uint64_t upto) {
     return 0;
 }
 
-/* Same layout rules as ref src/quant.c:182-213: header, tokenizer blob at 256,
+/* Same layout rules as ref src/quant.c:86-117: header, tokenizer blob at 256,
  * table 8-aligned after it, data region and every tensor 64-aligned. */
 int ember_quantize_file(const char *in_path, const char *out_path, int target) {
     EmberModel *m = ember_model_load(in_path);

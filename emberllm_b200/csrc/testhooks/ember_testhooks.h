@@ -1,0 +1,23 @@
+/* ember_testhooks.h — entry points of libember_testhooks.so, a TEST-ONLY library
+ * built beside the product (emberllm_b200/libember_testhooks.so). They run
+ * device helpers of the product's kernels in isolation for the tests; nothing in
+ * the product links or calls them, and they are not part of the C-ABI boundary.
+ * Each returns 0 on success. */
+#ifndef EMBER_TESTHOOKS_H
+#define EMBER_TESTHOOKS_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The decode GEMVs' RMSNorm sum (split_chain_sum) on `count` vectors of n
+ * non-negative terms each (host arrays, n <= 32768): host_out[i] = the terms
+ * added in index order from 0, host_hit[i] = 1 where the split evaluation
+ * answered (0: the rest was added sequentially). */
+int ember_cuda_split_sum_batch(const float *host_terms, int n, int count, float *host_out, int *host_hit);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

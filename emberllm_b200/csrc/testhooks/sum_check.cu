@@ -1,8 +1,10 @@
-// sum_check.cu — runs split_chain_sum (the RMSNorm sum of squares of the decode
-// GEMVs) on a batch of vectors, for the tests: one 256-thread block per vector,
-// reporting the sum and whether the split evaluation answered or the second
-// half was added after the first.
-#include "common.cuh"
+// sum_check.cu — TEST HOOK, built into libember_testhooks.so only (never into
+// the product library): runs split_chain_sum (the RMSNorm sum of squares of the
+// decode GEMVs, csrc/cuda/common.cuh) on a batch of vectors, one 256-thread block
+// per vector, reporting the sum and whether the split evaluation answered or the
+// rest was added sequentially.
+#include "cuda/common.cuh"
+#include "ember_testhooks.h"
 
 namespace emb {
 

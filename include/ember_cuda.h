@@ -124,9 +124,13 @@ int  ember_cuda_time_kernel(EmberCudaState *s, int kind, int reps, float *ms_per
  * risk cudaMalloc's synchronisation): it takes only caller-owned buffers and
  * keeps its scratch in a fixed array inside the library (about 2 KB per device,
  * held until exit). n must be in [1, 67108864]; other sizes are rejected with
- * status 1 and a line on stderr (2: bad pointer, 3: CUDA error). The first call
- * on a device looks the array up and should come before any stream capture;
- * calls that overlap on the GPU share the array and race. */
+ * status 1 and a line on stderr (2: bad pointer -- logits and out_index must be
+ * device memory of one device, and a non-NULL stream must belong to it; 3: CUDA
+ * error). The pick follows the reference's loop exactly: a NaN never wins, and a
+ * NaN at index 0 gives 0. The work runs on the logits' device; the caller's
+ * current device is unchanged on return. The first call on a device looks the
+ * array up and should come before any stream capture; calls that overlap on the
+ * GPU share the array and race. */
 int  ember_cuda_argmax_static(const float *logits, int n, int *out_index, void *stream);
 
 /* ---- batched greedy decode of independent streams ----
@@ -174,12 +178,6 @@ int          ember_cuda_available(void);
 int  ember_host_expf_params(EmberExpfParams *out);
 /* the device recipe evaluated on the host (identical bits); for tests */
 float ember_host_expf_emulated(const EmberExpfParams *p, float x);
-/* The decode GEMVs' RMSNorm sum (split_chain_sum) on `count` vectors of n
- * non-negative terms each (host arrays, n <= 32768): host_out[i] = the terms
- * added in index order from 0, host_hit[i] = 1 where the split evaluation
- * answered (0: the second half was added after the first). 0 on success. For
- * tests. */
-int ember_cuda_split_sum_batch(const float *host_terms, int n, int count, float *host_out, int *host_hit);
 /* fills [ctx][hd/2][2] with the reference's cos/sin values */
 void ember_host_rope_table(float *out, int ctx, int head_dim, float theta);
 

@@ -1,6 +1,7 @@
 """Test helpers: build-on-demand and ctypes access to the three libraries.
 
   product   emberllm_b200/libember_b200.so      (the thing under test)
+  hooks     emberllm_b200/libember_testhooks.so (device helpers run alone, test-only)
   oracle    oracle/liboracle.so                 (our C restatement, test-only)
   reference oracle/_ref/libember_ref_det.so     (emberllm compiled from its own
                                                  sources with its deterministic
@@ -14,6 +15,7 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB = os.path.join(ROOT, "emberllm_b200", "libember_b200.so")
+HOOKS = os.path.join(ROOT, "emberllm_b200", "libember_testhooks.so")
 ORACLE = os.path.join(ROOT, "oracle", "liboracle.so")
 REF_DET = os.path.join(ROOT, "oracle", "_ref", "libember_ref_det.so")
 
@@ -23,12 +25,19 @@ _IP = ctypes.POINTER(ctypes.c_int)
 
 
 def ensure_built():
-    if not os.path.exists(LIB):
+    if not os.path.exists(LIB) or not os.path.exists(HOOKS):
         subprocess.run(["make", "-C", os.path.join(ROOT, "emberllm_b200"), "-j8"], check=True,
                        stdout=subprocess.DEVNULL)
     if not os.path.exists(ORACLE):
         subprocess.run(["make", "-C", os.path.join(ROOT, "oracle"), "oracle"], check=True,
                        stdout=subprocess.DEVNULL)
+
+
+def reference_dir():
+    """the reference source tree's location: oracle/Makefile's REF variable"""
+    r = subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "print-ref"], capture_output=True,
+                       text=True)
+    return r.stdout.strip() if r.returncode == 0 else ""
 
 
 def have_reference():
@@ -183,3 +192,12 @@ def greedy_run(sess, prompt, n):
         logits = sess.forward(t, pos)
         pos += 1
     return out
+
+
+def testhooks():
+    """libember_testhooks.so with its prototypes (test infrastructure)"""
+    ensure_built()
+    lib = ctypes.CDLL(HOOKS)
+    lib.ember_cuda_split_sum_batch.restype = ctypes.c_int
+    lib.ember_cuda_split_sum_batch.argtypes = [_P, ctypes.c_int, ctypes.c_int, _P, _P]
+    return lib

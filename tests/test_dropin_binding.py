@@ -1,4 +1,4 @@
-"""The drop-in recipes of INTEGRATION.md, checked on CPU. emberllm's own front-end
+"""The drop-in recipes for emberllm's callers, checked on CPU. emberllm's own front-end
 sources (tokenizer, sampler, JSON, server) link against this library into a
 `libember.so`, and emberllm's unmodified Python binding (bindings/python/
 emberllm.py) loads it through EMBER_LIB: model header and tokenizer round trip
@@ -15,8 +15,10 @@ import pytest
 
 from emberllm_b200 import synth
 
+from . import helpers as H
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF_SRC = os.environ.get("REF", "/root/reference")   # as oracle/Makefile's REF
+REF_SRC = H.reference_dir()   # oracle/Makefile's REF
 REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libember_ref_det.so")
 B200 = os.path.join(ROOT, "emberllm_b200")
 
@@ -72,8 +74,8 @@ def test_reference_binding_runs_on_the_dropin_library(dropin, name):
 
 @pytest.fixture(scope="module")
 def cli(tmp_path_factory):
-    """emberllm's CLI linked as INTEGRATION.md's Makefile does: its front-end
-    sources and this library"""
+    """emberllm's CLI linked against this library: its front-end sources
+    (main.c, tokenizer, sampler, JSON, server) and libember_b200"""
     out = tmp_path_factory.mktemp("cli") / "ember"
     src = [os.path.join(REF_SRC, "src", f) for f in ("main.c", "tokenizer.c", "sample.c", "json.c", "server.c")]
     r = subprocess.run(["gcc", "-std=c11", "-D_DEFAULT_SOURCE", "-O2", "-o", str(out), *src, "-L" + B200,

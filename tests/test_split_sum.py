@@ -10,8 +10,6 @@ answer."""
 import numpy as np
 import pytest
 
-from emberllm_b200 import _lib
-
 from . import helpers as H
 
 pytestmark = pytest.mark.gpu
@@ -19,8 +17,7 @@ pytestmark = pytest.mark.gpu
 
 @pytest.fixture(scope="module")
 def lib():
-    H.ensure_built()
-    return _lib.load()
+    return H.testhooks()
 
 
 def seq_sum(terms):
