@@ -85,6 +85,41 @@ EMB_DEV uint32_t quant_quad(float4 v, unsigned mask, float *dq) {
     return packed;
 }
 
+// int8 dot of one Q8_0 weight block (32 B) with one activation block, both in smem
+EMB_DEV int dot_q8_block(const uint8_t *w, const int8_t *xq) {
+    int4 w0 = reinterpret_cast<const int4 *>(w)[0];
+    int4 w1 = reinterpret_cast<const int4 *>(w)[1];
+    int4 a0 = reinterpret_cast<const int4 *>(xq)[0];
+    int4 a1 = reinterpret_cast<const int4 *>(xq)[1];
+    int acc = 0;
+    acc = __dp4a(w0.x, a0.x, acc); acc = __dp4a(w0.y, a0.y, acc);
+    acc = __dp4a(w0.z, a0.z, acc); acc = __dp4a(w0.w, a0.w, acc);
+    acc = __dp4a(w1.x, a1.x, acc); acc = __dp4a(w1.y, a1.y, acc);
+    acc = __dp4a(w1.z, a1.z, acc); acc = __dp4a(w1.w, a1.w, acc);
+    return acc;
+}
+
+// Q4_0 block (16 B): element i is nibble (byte i & 15) - 8, element i+16 is
+// (byte i >> 4) - 8 (ref src/kernels.c:175-179). Unsigned nibbles fit in a
+// signed byte, so sum((n-8)*a) = sum(n*a) - 8*sum(a), all exact in int32.
+EMB_DEV int dot_q4_block(const uint8_t *w, const int8_t *xq) {
+    uint4 v = reinterpret_cast<const uint4 *>(w)[0];
+    int4 a0 = reinterpret_cast<const int4 *>(xq)[0];
+    int4 a1 = reinterpret_cast<const int4 *>(xq)[1];
+    const uint32_t m = 0x0F0F0F0Fu;
+    int acc = 0;
+    acc = __dp4a((int)(v.x & m), a0.x, acc); acc = __dp4a((int)(v.y & m), a0.y, acc);
+    acc = __dp4a((int)(v.z & m), a0.z, acc); acc = __dp4a((int)(v.w & m), a0.w, acc);
+    acc = __dp4a((int)((v.x >> 4) & m), a1.x, acc); acc = __dp4a((int)((v.y >> 4) & m), a1.y, acc);
+    acc = __dp4a((int)((v.z >> 4) & m), a1.z, acc); acc = __dp4a((int)((v.w >> 4) & m), a1.w, acc);
+    int sa = 0;
+    const int ones = 0x01010101;
+    sa = __dp4a(a0.x, ones, sa); sa = __dp4a(a0.y, ones, sa); sa = __dp4a(a0.z, ones, sa);
+    sa = __dp4a(a0.w, ones, sa); sa = __dp4a(a1.x, ones, sa); sa = __dp4a(a1.y, ones, sa);
+    sa = __dp4a(a1.z, ones, sa); sa = __dp4a(a1.w, ones, sa);
+    return acc - 8 * sa;
+}
+
 // Bytes of one row in the device layout: Q8_0 32 int8 per block, Q4_0 16 bytes
 // per block, fp32 4 bytes per element.
 __host__ __device__ inline size_t qrow_bytes(int dtype, int cols) {

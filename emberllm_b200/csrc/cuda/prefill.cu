@@ -653,6 +653,9 @@ extern "C" int ember_cuda_batch_new(EmberCudaModel *m, int n_streams, int ctx, i
             EmberCudaState *r = nullptr;
             rc = ember_cuda_state_new(m, ctx, b->kv_fp16, rope_cs, &r);
             if (!rc) b->reps.push_back(r);
+            // the replicas run at once on their own streams: the graph step, not the
+            // persistent kernel (which takes every SM)
+            if (!rc) persist_release(r);
             if (!rc) rc = greedy_prepare(r);
         }
         if (rc) {

@@ -219,6 +219,7 @@ extern "C" uint64_t ember_cuda_model_bytes(const EmberCudaModel *m) { return m ?
 
 static void state_release(EmberCudaState *s) {
     pf_state_release(s);
+    persist_release(s);
     if (s->g_fwd) cudaGraphExecDestroy(s->g_fwd);
     if (s->g_greedy) cudaGraphExecDestroy(s->g_greedy);
     if (s->g_prefill) cudaGraphExecDestroy(s->g_prefill);
@@ -331,6 +332,12 @@ extern "C" int ember_cuda_state_new(EmberCudaModel *m, int ctx, int kv_fp16, con
                 delete s;
                 return 1;
             }
+    }
+    // the token step as one persistent kernel where the model and context suit it
+    if (persist_init(s)) {
+        state_release(s);
+        delete s;
+        return 1;
     }
     *out = s;
     return 0;
@@ -700,16 +707,28 @@ static int check_device_error(EmberCudaState *s, int err) {
     if (err == ERR_NONE) return 0;
     cudaMemsetAsync(s->ctl + CTL_ERR, 0, sizeof(int), s->stream);
     cudaStreamSynchronize(s->stream);
-    return set_err("device wait timed out (code %d): a bulk copy never completed", err);
+    const char *what = err == 11 ? "a hand-off between CTAs of the persistent step never arrived"
+                       : err == 12 ? "a weight copy of the persistent step never completed"
+                       : err == 13 ? "a cache copy of the persistent step never completed"
+                                   : "a bulk copy never completed";
+    return set_err("device wait timed out (code %d): %s", err, what);
 }
 
 extern "C" int ember_cuda_forward(EmberCudaState *s, int tok, int pos, float *host_logits) {
     CK(cudaSetDevice(s->m->device));
-    if (!s->g_fwd && capture(s, &s->g_fwd, 0)) return 1;
     s->h_ctl[CTL_POS] = pos;
     s->h_ctl[CTL_TOK] = tok;
     s->h_ctl[CTL_ERR] = 0;
-    CK(cudaGraphLaunch(s->g_fwd, s->stream));
+    if (s->ps) {
+        // one step of the persistent kernel; the logits and the error word back
+        CK(cudaMemcpyAsync(s->ctl, s->h_ctl, 2 * sizeof(int), cudaMemcpyHostToDevice, s->stream));
+        if (persist_run(s, 1, 0)) return 1;
+        CK(cudaMemcpyAsync(s->h_logits, s->logits, (size_t)s->m->vocab * 4, cudaMemcpyDeviceToHost, s->stream));
+        CK(cudaMemcpyAsync(s->h_ctl + CTL_ERR, s->ctl + CTL_ERR, sizeof(int), cudaMemcpyDeviceToHost, s->stream));
+    } else {
+        if (!s->g_fwd && capture(s, &s->g_fwd, 0)) return 1;
+        CK(cudaGraphLaunch(s->g_fwd, s->stream));
+    }
     CK(cudaStreamSynchronize(s->stream));
     if (check_device_error(s, s->h_ctl[CTL_ERR])) return 1;
     if (host_logits && host_logits != s->h_logits) memcpy(host_logits, s->h_logits, (size_t)s->m->vocab * 4);
@@ -778,12 +797,16 @@ int emb::greedy_prepare(EmberCudaState *s) {
 // feeds t_i at pos + i (t_0 = tok); the chosen tokens go to host_tokens (pinned
 // memory, or the copy synchronises) once the steps are done.
 int emb::greedy_enqueue(EmberCudaState *s, int tok, int pos, int n_steps, int *host_tokens) {
-    if (greedy_prepare(s)) return 1;
+    if (!s->ps && greedy_prepare(s)) return 1;
     int *hc = s->h_ctl;
     CK(cudaStreamSynchronize(s->stream));
     hc[CTL_POS] = pos; hc[CTL_TOK] = tok; hc[CTL_NOUT] = 0; hc[CTL_BASE] = 0; hc[CTL_ERR] = 0;
     CK(cudaMemcpyAsync(s->ctl, hc, 5 * sizeof(int), cudaMemcpyHostToDevice, s->stream));
-    for (int i = 0; i < n_steps; i++) CK(cudaGraphLaunch(s->g_greedy, s->stream));
+    if (s->ps) {
+        if (persist_run(s, n_steps, 1)) return 1;   // the whole run in one launch
+    } else {
+        for (int i = 0; i < n_steps; i++) CK(cudaGraphLaunch(s->g_greedy, s->stream));
+    }
     if (host_tokens) CK(cudaMemcpyAsync(host_tokens, s->out_tokens, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, s->stream));
     return 0;
 }

@@ -43,6 +43,7 @@ struct DevLayer {
 namespace emb {
 struct PfModel;   // batched-prefill weight packs (prefill.cu), built on first use
 struct PfState;   // batched-prefill activations (prefill.cu), built on first use
+struct PState;    // the persistent token step's plan and hand-off buffers (persist.cu)
 }  // namespace emb
 
 struct EmberCudaModel {
@@ -99,6 +100,7 @@ struct EmberCudaState {
     cudaGraphExec_t g_fwd = nullptr, g_greedy = nullptr, g_prefill = nullptr, g_head = nullptr;
     int launches_per_step = 0;
     emb::PfState *pf = nullptr;
+    emb::PState *ps = nullptr;             // set when the persistent token step serves this state
 };
 
 static inline int salloc(EmberCudaState *s, void **p, size_t n) {
@@ -114,6 +116,17 @@ namespace emb {
 int greedy_prepare(EmberCudaState *s);
 int greedy_enqueue(EmberCudaState *s, int tok, int pos, int n_steps, int *host_tokens);
 int greedy_finish(EmberCudaState *s);
+}  // namespace emb
+
+// ---- the persistent token step (persist.cu) ----
+namespace emb {
+// Sets s->ps when the state's model and context suit the persistent step
+// (returns 0 and leaves s->ps NULL otherwise); 1 on a CUDA error.
+int persist_init(EmberCudaState *s);
+void persist_release(EmberCudaState *s);
+// enqueue n_steps token steps from ctl's token and position on s->stream;
+// greedy: pick between steps and write the picks to s->out_tokens
+int persist_run(EmberCudaState *s, int n_steps, int greedy);
 }  // namespace emb
 
 // ---- batched prefill (prefill.cu) ----

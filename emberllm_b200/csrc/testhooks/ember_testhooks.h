@@ -16,6 +16,10 @@ extern "C" {
  * answered (0: the rest was added sequentially). */
 int ember_cuda_split_sum_batch(const float *host_terms, int n, int count, float *host_out, int *host_hit);
 
+/* The persistent token step's 512-thread sum (psum: up to 16 segments) on
+ * `count` vectors of n non-negative terms (n a multiple of 16, <= 32768). */
+int ember_cuda_psum_batch(const float *host_terms, int n, int count, float *host_out);
+
 #ifdef __cplusplus
 }
 #endif

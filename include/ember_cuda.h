@@ -167,6 +167,10 @@ float       *ember_cuda_state_host_logits(EmberCudaState *s);
 void        *ember_cuda_state_stream(EmberCudaState *s);      /* cudaStream_t */
 const float *ember_cuda_state_logits_dev(EmberCudaState *s);  /* device pointer */
 int          ember_cuda_state_launches_per_step(const EmberCudaState *s);
+/* 1 when the state's decode steps run as the persistent kernel (one cooperative
+ * launch per forward step or greedy run); 0 when they run as captured graphs of
+ * per-stage kernels, with *why (if not NULL) naming the reason */
+int          ember_cuda_state_persistent(const EmberCudaState *s, const char **why);
 const char  *ember_cuda_error(void);
 /* 1 if this library was built with sm_100a device code and a device is usable */
 int          ember_cuda_available(void);

@@ -200,4 +200,6 @@ def testhooks():
     lib = ctypes.CDLL(HOOKS)
     lib.ember_cuda_split_sum_batch.restype = ctypes.c_int
     lib.ember_cuda_split_sum_batch.argtypes = [_P, ctypes.c_int, ctypes.c_int, _P, _P]
+    lib.ember_cuda_psum_batch.restype = ctypes.c_int
+    lib.ember_cuda_psum_batch.argtypes = [_P, ctypes.c_int, ctypes.c_int, _P]
     return lib

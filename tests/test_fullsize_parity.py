@@ -105,3 +105,17 @@ def test_smollm2_q4_prefill512_greedy256(prod, orc):
     prompt = _prompt(49152, 512)
     want = _run(prod, orc, "smollm2-135m", 512 + 256 + 8, 0, prompt, 256)
     assert _device_greedy("smollm2-135m", 512 + 256 + 8, 0, prompt, 256) == want
+
+
+@pytest.mark.parametrize("name,ctx,want", [("qwen3-0.6b", 264, 1), ("qwen2.5-0.5b", 648, 1),
+                                           ("smollm2-135m", 776, 1), ("stories110m", 264, 1),
+                                           ("qwen3-0.6b", 1048, 0)])
+def test_which_decode_path_serves_each_config(prod, name, ctx, want):
+    """the BASELINE decode configurations run as the persistent kernel (the bench
+    workload included); contexts whose keys exceed shared memory keep the graph
+    step with the split attention"""
+    from .test_gpu_parity import is_persistent
+    a = prod.session(synth.ensure_model(name), ctx, 0)
+    got, why = is_persistent(prod.lib, a)
+    a.close()
+    assert got == want, why

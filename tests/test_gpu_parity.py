@@ -47,16 +47,34 @@ def orc():
     return H.Oracle()
 
 
-@pytest.mark.parametrize("attn", ["fused", "split"])
+def is_persistent(lib, sess):
+    """whether a product session's decode runs as the persistent kernel"""
+    lib.ember_state_cuda.restype = ctypes.c_void_p
+    lib.ember_state_cuda.argtypes = [ctypes.c_void_p]
+    lib.ember_cuda_state_persistent.restype = ctypes.c_int
+    lib.ember_cuda_state_persistent.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_char_p)]
+    why = ctypes.c_char_p()
+    return lib.ember_cuda_state_persistent(lib.ember_state_cuda(sess.s), ctypes.byref(why)) == 1, why.value
+
+
+@pytest.mark.parametrize("attn", ["fused", "split", "persistent"])
 @pytest.mark.parametrize("kv16", [0, 1])
 @pytest.mark.parametrize("name", TINY)
 def test_tiny_teacher_forced_bitexact(prod, orc, name, kv16, attn, monkeypatch):
-    """prefill 24 random ids, then 40 forced forwards: every step's logits equal
-    (both decode attention paths: one kernel per head, and the cache split over
-    CTAs)"""
-    monkeypatch.setenv("EMBER_ATTN", attn)
+    """prefill 24 random ids, then 40 forced forwards: every step's logits equal,
+    on each decode path: the captured graphs with one attention kernel per head
+    or with the cache split over CTAs, and the persistent kernel (quantized
+    models)"""
+    if attn == "persistent":
+        if name == "tiny-f32":
+            pytest.skip("the persistent step serves quantized models")
+        monkeypatch.setenv("EMBER_PERSIST", "1")
+    else:
+        monkeypatch.setenv("EMBER_PERSIST", "0")
+        monkeypatch.setenv("EMBER_ATTN", attn)
     path = synth.ensure_model(name)
     a = prod.session(path, 0, kv16)
+    assert is_persistent(prod.lib, a)[0] == (attn == "persistent"), is_persistent(prod.lib, a)
     b = orc.session(path, 0, kv16)
     rng = np.random.default_rng(7)
     ids = rng.integers(0, a.vocab, 24)
@@ -68,9 +86,12 @@ def test_tiny_teacher_forced_bitexact(prod, orc, name, kv16, attn, monkeypatch):
     b.close()
 
 
+@pytest.mark.parametrize("persist", ["0", "1"])
 @pytest.mark.parametrize("name", TINY)
-def test_tiny_device_greedy_matches_oracle(prod, orc, name):
-    """device-side greedy loop (ember_forward_greedy) = oracle's greedy"""
+def test_tiny_device_greedy_matches_oracle(prod, orc, name, persist, monkeypatch):
+    """device-side greedy loop (ember_forward_greedy) = oracle's greedy, on the
+    graph step and on the persistent kernel (one launch for the whole run)"""
+    monkeypatch.setenv("EMBER_PERSIST", persist)
     from emberllm_b200 import Ember
     path = synth.ensure_model(name)
     rng = np.random.default_rng(3)

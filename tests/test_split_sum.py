@@ -96,3 +96,24 @@ def test_split_sum_random_sweep(lib):
         for i, t in enumerate(vecs):
             assert out[i].view(np.uint32) == seq_sum(t).view(np.uint32), (n, i)
         assert hit[np.array(mild)].mean() > 0.97, (n, hit[np.array(mild)].mean())
+
+
+@pytest.mark.parametrize("n", [64, 128, 256, 576, 768, 896, 1024, 2048, 4096])
+def test_persistent_step_sum_matches_the_loop(lib, n):
+    """the persistent step's 512-thread variant (psum: 16, 8 or 4 segments by n,
+    float tree estimates) equals the sequential float loop bit for bit on every
+    case above, including the outliers that send it to its sequential fallback"""
+    rng = np.random.default_rng(n + 7)
+    vecs = []
+    for rep in range(4):
+        vecs += [t for _, t in squares(rng, n)]
+        x = (rng.standard_normal(n) * (2.0 + 3 * rep)).astype(np.float32)
+        vecs.append(np.exp((x - x.max()).astype(np.float64)).astype(np.float32))
+    for k in range(100):
+        x = (rng.standard_normal(n) * np.exp(rng.uniform(-20, 20)) * np.exp(rng.standard_normal(n) * (k % 5))).astype(np.float32)
+        vecs.append((x * x).astype(np.float32))
+    v = np.ascontiguousarray(np.stack(vecs), dtype=np.float32)
+    out = np.zeros(len(vecs), np.float32)
+    assert lib.ember_cuda_psum_batch(v.ctypes.data, n, len(vecs), out.ctypes.data) == 0
+    for i, t in enumerate(vecs):
+        assert out[i].view(np.uint32) == seq_sum(t).view(np.uint32), (n, i)
