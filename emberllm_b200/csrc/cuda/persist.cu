@@ -102,6 +102,7 @@ int emb::persist_init(EmberCudaState *s) {
     a.rope = s->rope; a.logits = s->logits; a.ctl = s->ctl;
     a.ex = m->ex;
     a.spin_limit = (uint32_t)env_int("EMBER_WAIT_POLLS", 1 << 22);
+    a.poll_ns = (uint32_t)env_int("EMBER_POLL_NS", 200);
     // pieces
     a.rp_qkv = rows_per_piece(a.wdtype, m->dim, 1, 32);
     a.rp_wo = rows_per_piece(a.wdtype, qd, 1, 32);

@@ -105,6 +105,7 @@ struct PArgs {
     unsigned long long *w_am;    // [2 * GEMV CTAs] argmax partials (value, index)
     int n_steps;
     uint32_t spin_limit;       // polls before a hand-off wait gives up
+    uint32_t poll_ns;          // pause between polls of a hand-off word
     // attention shared-memory plan
     int kcap;                  // cached positions the key region holds ([hd][kcap])
     int vcap0;                 // positions the value region holds
@@ -126,9 +127,18 @@ __device__ unsigned long long g_pp[4][P_MAXL + 1][16];
     do {                                                                                    \
         if (threadIdx.x == 0 && (role) >= 0 && probe_on) g_pp[role][l][ev] = probe_now(); \
     } while (0)
+// finer probes inside one S1 stage and one norm (layer 1, first GEMV CTA)
+__shared__ int p_detail;
+#define PDETAIL(ev)                                                                  \
+    do {                                                                             \
+        if (threadIdx.x == 0 && p_detail) g_pp[0][P_MAXL][ev] = probe_now();          \
+    } while (0)
 #else
 #define PPROBE(role, l, ev) \
     do {                    \
+    } while (0)
+#define PDETAIL(ev) \
+    do {            \
     } while (0)
 #endif
 
@@ -302,6 +312,7 @@ EMB_DEV bool tw_wait(uint32_t (&vals)[MAXW], const unsigned long long *src, int 
                 break;
             }
         }
+        if (missing && a.poll_ns) __nanosleep(a.poll_ns);
     }
     return !__syncthreads_or(fail);
 }
@@ -319,6 +330,7 @@ EMB_DEV bool tw_wait1(uint32_t *val, const unsigned long long *p, uint32_t tag, 
                 if (ld_err(err) != 0) { fail = true; break; }
                 if (it >= a.spin_limit) { atomicExch(err, ERR_P_HANDOFF); fail = true; break; }
             }
+            if (a.poll_ns) __nanosleep(a.poll_ns);
         }
     }
     return !__syncthreads_or(fail);
@@ -536,12 +548,16 @@ EMB_DEV bool gather_q8(const PArgs &a, int8_t *xq, float *xd, const unsigned lon
 // memory, copied there by this CTA's cp.async group before the newest one.
 EMB_DEV void norm_quant(const PArgs &a, float *xf, float *sq, int8_t *xq, float *xd, const float *w_s) {
     const int n = a.dim, nb = n / 32;
+    PDETAIL(6);
     cp_async_wait_1();
     for (int i = threadIdx.x; i < n; i += PT) sq[i] = fmul(xf[i], xf[i]);
     __syncthreads();
+    PDETAIL(7);
     const float sc = rms_scale(psum(sq, n), n, a.eps);
+    PDETAIL(8);
     for (int i = threadIdx.x; i < n; i += PT) xf[i] = fmul(fmul(xf[i], sc), w_s[i]);
     __syncthreads();
+    PDETAIL(9);
     for (int base = 0; base < nb * 8; base += PT) {
         const int q8 = base + (int)threadIdx.x;
         const bool act = q8 < nb * 8;
@@ -555,6 +571,7 @@ EMB_DEV void norm_quant(const PArgs &a, float *xf, float *sq, int8_t *xq, float 
         }
     }
     __syncthreads();
+    PDETAIL(10);
 }
 
 }  // namespace emb
@@ -590,8 +607,10 @@ EMB_DEV bool gemv_stage(const PArgs &a, const PieceTab &t, GShared &g, const GVi
     int hb_i = 0x7FFFFFFF;
     for (int i = 0; i < t.n[ST]; i++) {
         const Piece pc = t.p[t.first[ST] + i];
+        if (ST == PS_QKV && i == 0) PDETAIL(0);
         const unsigned char *slot = ring_acquire(a, g, v.ring);
         if (!slot) return false;
+        if (ST == PS_QKV && i == 0) PDETAIL(1);
         const uint8_t *q;
         const __half *s;
         int cols, dtype;
@@ -620,7 +639,29 @@ EMB_DEV bool gemv_stage(const PArgs &a, const PieceTab &t, GShared &g, const GVi
                 pr[b] = fmul(fmul(__int2float_rn(acc), __half2float(ws[b])), v.xd[b]);
             }
         }
+        if (ST == PS_QKV && i == 0) PDETAIL(2);
+#ifdef EMBER_PROBES
+        if (ST == PS_QKV && i == 0 && p_detail) {
+            // the same dot loop once more, now warm, for the probe timeline
+            __syncthreads();
+            PDETAIL(11);
+            for (int rr = warp; rr < rows; rr += PNW) {
+                const int sub = nsub == 2 && rr >= nr ? 1 : 0, r = rr - sub * nr;
+                const uint8_t *wq = slot + sub * qbytes + (size_t)r * qrb;
+                const __half *ws = (sub ? sc_b : sc_a) + r * nb;
+                float *pr = v.P + rr * pstride;
+                for (int b = lane; b < nb; b += 32) {
+                    const int acc = dtype == EMBER_DT_Q8_0 ? dot_q8_block(wq + b * 32, v.xq + b * 32)
+                                                           : dot_q4_block(wq + b * 16, v.xq + b * 32);
+                    pr[b] = fmul(fmul(__int2float_rn(acc), __half2float(ws[b])), v.xd[b]);
+                }
+            }
+            __syncthreads();
+            PDETAIL(12);
+        }
+#endif
         ring_release(a, t, g, v.ring);   // every warp is past the slot
+        if (ST == PS_QKV && i == 0) PDETAIL(3);
         // chains and epilogue: row rr = warp + 16 * lane on lanes 0..3
         const int rr = warp + PNW * lane;
         if (lane < 4 && rr < rows) {
@@ -643,6 +684,7 @@ EMB_DEV bool gemv_stage(const PArgs &a, const PieceTab &t, GShared &g, const GVi
                 if (y == y && am_better(y, row, hb_v, hb_i)) { hb_v = y; hb_i = row; }   // NaN never wins
             }
         }
+        if (ST == PS_QKV && i == 0) PDETAIL(4);
         if (ST == PS_W13) {
             // h = SiLU(g) * u = g / (1 + expf(-g)) * u (ref src/model.c:403-406)
             __syncthreads();
@@ -1088,11 +1130,18 @@ EMB_DEV bool gemv_cta(const PArgs &a, unsigned char *smem, double *tab, int gi, 
             if (l > 0) ok = gather_x(a, v.xf, a.w_x + a.dim, TL - 8u + TG_XB);
             if (!ok) break;
             PPROBE(role, l, 1);
+#ifdef EMBER_PROBES
+            if (tid == 0) p_detail = probe_on && role == 0 && l == 1;
+            __syncthreads();
+#endif
             for (int r = v.own0 + tid; r < v.own1; r += PT) v.xown[r - v.own0] = v.xf[r];
             norm_quant(a, v.xf, v.sq, v.xq, v.xd, nw);
             PPROBE(role, l, 2);
             ok = gemv_stage<PS_QKV>(a, t, g, v, l, TL + TG_QKV);
             PPROBE(role, l, 3);
+#ifdef EMBER_PROBES
+            if (tid == 0) p_detail = 0;
+#endif
             ok = ok && gather_q8(a, v.xq, v.xd, a.w_o, qd, TL + TG_O);
             PPROBE(role, l, 4);
             ok = ok && gemv_stage<PS_WO>(a, t, g, v, l, TL + TG_XA);
