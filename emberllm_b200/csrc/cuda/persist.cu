@@ -46,7 +46,9 @@ static int rows_per_piece(int dtype, int cols, int nmat, int cap) {
 // Why a state cannot take the persistent path, or NULL when it can.
 static const char *persist_blocker(const EmberCudaState *s) {
     const EmberCudaModel *m = s->m;
-    if (env_int("EMBER_PERSIST", 1) == 0) return "EMBER_PERSIST=0";
+    // opt-in: measured slower than the graph step on B200 (its per-stage
+    // latencies exceed the launch overheads it saves)
+    if (env_int("EMBER_PERSIST", 0) == 0) return "not requested (EMBER_PERSIST=1 selects it)";
     const int dt = m->layers.empty() ? -1 : m->layers[0].wq.dtype;
     if (dt != EMBER_DT_Q8_0 && dt != EMBER_DT_Q4_0) return "layer weights are not Q8_0/Q4_0";
     for (const DevLayer &L : m->layers) {
@@ -57,7 +59,7 @@ static const char *persist_blocker(const EmberCudaState *s) {
     if (m->tok_emb.dtype != EMBER_DT_Q8_0) return "the embedding is not Q8_0";
     if (m->lm_head.dtype != EMBER_DT_Q8_0 && m->lm_head.dtype != EMBER_DT_Q4_0) return "lm_head is not quantized";
     const int hd = m->head_dim, qd = m->n_heads * hd, G = m->n_sm - m->n_heads;
-    if (m->dim % 32 || m->hidden % 32 || hd % 32 || hd > 256 || m->n_heads % m->n_kv) return "shapes";
+    if (m->dim % 32 || m->hidden % 32 || hd % 32 || 3 * hd > PT || m->n_heads % m->n_kv) return "shapes";
     if (m->dim > 4 * PT || qd / 4 + qd / 32 > 4 * PT || m->hidden / 4 + m->hidden / 32 > 4 * PT) return "too wide";
     if (m->n_heads > m->n_sm / 2) return "too many heads for the SMs";
     if (m->n_layers > P_MAXL) return "too many layers";
@@ -158,10 +160,10 @@ int emb::persist_init(EmberCudaState *s) {
     int occ = 0;
     if (s->kv_fp16) {
         CK(cudaFuncSetAttribute(ember_persist_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn));
-        CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ember_persist_kernel<__half>, PT, dyn));
+        CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ember_persist_kernel<__half>, PTT, dyn));
     } else {
         CK(cudaFuncSetAttribute(ember_persist_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn));
-        CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ember_persist_kernel<float>, PT, dyn));
+        CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ember_persist_kernel<float>, PTT, dyn));
     }
     int coop = 0;
     CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->device));
@@ -230,7 +232,7 @@ int emb::persist_run(EmberCudaState *s, int n_steps, int greedy) {
     a.out_tokens = greedy ? s->out_tokens : nullptr;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ps->grid);
-    cfg.blockDim = dim3((unsigned)PT);
+    cfg.blockDim = dim3((unsigned)PTT);
     cfg.dynamicSmemBytes = ps->smem;
     cfg.stream = s->stream;
     cudaLaunchAttribute attr[1];

@@ -43,8 +43,25 @@
 
 namespace emb {
 
-constexpr int PT = 512;                 // threads per CTA
+constexpr int PT = 480;                 // compute threads per CTA (warps 0-14)
 constexpr int PNW = PT / 32;
+constexpr int PTT = PT + 32;            // + one producer warp (GEMV CTAs: issues the weight copies)
+
+// barriers among the compute threads only (named barrier 1), so that the
+// producer warp never takes part
+EMB_DEV void csync() { asm volatile("bar.sync 1, 480;" ::: "memory"); }
+EMB_DEV bool csync_or(bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred a, b;\n\t"
+        "setp.ne.u32 a, %1, 0;\n\t"
+        "bar.red.or.pred b, 1, 480, a;\n\t"
+        "selp.u32 %0, 1, 0, b;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)p)
+        : "memory");
+    return r != 0;
+}
 constexpr int P_NSLOT = 4;              // weight ring slots per GEMV CTA
 constexpr int P_SLOT = 36864;           // bytes per slot
 constexpr int P_MAXPIECES = 96;         // pieces of one stage per CTA (lm_head is the longest)
@@ -67,6 +84,12 @@ constexpr int P_MAXL = 48;              // layers the shared-memory pointer tabl
 // the per-layer pointers, copied into shared memory at the start of a launch so
 // that no stage waits on a global load for a pointer
 __shared__ PLayer p_layers[P_MAXL];
+
+// the dynamic shared memory of the persistent kernel. Every shared-memory
+// pointer of the step is derived from this symbol (never mixed with a null or
+// global pointer), so the compiler keeps shared-space loads and stores, which
+// are several times faster than generic ones.
+extern __shared__ __align__(128) unsigned char p_dyn[];
 
 // 4-byte global -> shared copy that completes asynchronously (cp.async); the
 // issuing thread waits for its groups with cp.async.wait_group
@@ -149,14 +172,14 @@ __shared__ int p_detail;
 // estimate of the sum before it; the boundaries walked in order, taking the
 // chain that started from the sum actually reached, and the rest added
 // sequentially where a sum falls outside its window -- sized for a 512-thread
-// CTA: up to 16 segments, each estimated by one warp as a float tree sum (any
+// CTA (480 compute threads): up to 16 segments, each estimated by one warp as a float tree sum (any
 // fixed order serves: the estimate only centres the windows). Exact by
 // construction; only the time depends on the windows. v: shared memory,
 // 16-byte aligned, n a multiple of 16 K. Called by every thread of the CTA.
 template <int K, int NC>
 EMB_DEV float psum_split(const float *v, int n) {
     constexpr int NB = K - 1;
-    static_assert(NB * NC + 1 <= PT && K <= PNW, "psum_split: too many chains");
+    static_assert(NB * NC + 1 <= PT && NB <= PNW, "psum_split: too many chains");
     __shared__ float p_seg[K];
     __shared__ uint32_t p_b0[NB];
     __shared__ int p_fin;
@@ -171,7 +194,7 @@ EMB_DEV float psum_split(const float *v, int n) {
         for (int o = 16; o > 0; o >>= 1) e = __fadd_rn(e, __shfl_xor_sync(0xffffffffu, e, o));
         if (lane == 0) p_seg[warp] = e;
     }
-    __syncthreads();
+    csync();
     // warp 0: running sums of the segments, the window starts
     if (warp == 0) {
         float run = lane < NB ? p_seg[lane] : 0.0f;
@@ -186,7 +209,7 @@ EMB_DEV float psum_split(const float *v, int n) {
         const unsigned ok = __ballot_sync(0xffffffffu, fin || lane >= NB);
         if (lane == 0) p_fin = ok == 0xffffffffu;
     }
-    __syncthreads();
+    csync();
     if (tid <= NC * NB) {
         const bool is_first = tid == NC * NB;
         const int kk = is_first ? 0 : tid / NC, j = tid % NC;
@@ -207,7 +230,7 @@ EMB_DEV float psum_split(const float *v, int n) {
         if (is_first) p_first = s;
         else p_cand[kk][j] = s;
     }
-    __syncthreads();
+    csync();
     float s = p_first;
     int done = 1;
     const bool fin = p_fin != 0;
@@ -221,20 +244,20 @@ EMB_DEV float psum_split(const float *v, int n) {
     }
     if (done == K) return s;
     if (tid == 0) p_answer = chain_sum(s, v + done * m, n - done * m);
-    __syncthreads();
+    csync();
     return p_answer;
 }
 
 // the sum in index order of n non-negative shared-memory terms (n a multiple of
 // 16; 16-byte aligned): the most segments that divide it
 EMB_DEV float psum(const float *v, int n) {
-    if (n % 256 == 0 && n >= 2048) return psum_split<16, 32>(v, n);
+    if (n % 256 == 0 && n >= 2048) return psum_split<16, 28>(v, n);
     if (n % 128 == 0 && n >= 256) return psum_split<8, 64>(v, n);
     if (n % 64 == 0 && n >= 128) return psum_split<4, 64>(v, n);
     __shared__ float p_small;
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) p_small = chain_sum(0.0f, v, n);
-    __syncthreads();
+    csync();
     return p_small;
 }
 
@@ -314,7 +337,7 @@ EMB_DEV bool tw_wait(uint32_t (&vals)[MAXW], const unsigned long long *src, int 
         }
         if (missing && a.poll_ns) __nanosleep(a.poll_ns);
     }
-    return !__syncthreads_or(fail);
+    return !csync_or(fail);
 }
 
 // Wait until the word at p (when not null) carries `tag`; its value to *val.
@@ -333,7 +356,7 @@ EMB_DEV bool tw_wait1(uint32_t *val, const unsigned long long *p, uint32_t tag, 
             if (a.poll_ns) __nanosleep(a.poll_ns);
         }
     }
-    return !__syncthreads_or(fail);
+    return !csync_or(fail);
 }
 
 // ---- weight pieces ---------------------------------------------------------------
@@ -377,16 +400,17 @@ namespace emb {
 
 // ---- the GEMV CTA's weight ring -------------------------------------------------
 // Slot k % P_NSLOT holds piece k of the CTA's piece sequence: per token step,
-// per layer the QKV, WO, W13 and W2 pieces, then the lm_head pieces. Thread 0
-// issues piece k + P_NSLOT as soon as piece k's slot is consumed.
+// per layer the QKV, WO, W13 and W2 pieces, then the lm_head pieces. One lane
+// of the producer warp issues piece k into its slot as soon as the 15 compute
+// warps have released piece k - P_NSLOT (each arrives on the slot's `empty`
+// barrier once it is past the slot); the compute warps wait on `full`.
 struct Cursor {
     int step, l, s, i;
 };
 
 struct GShared {
     uint64_t full[P_NSLOT];
-    Cursor ic;                 // next piece to issue
-    unsigned issued, consumed;
+    uint64_t empty[P_NSLOT];
     float bv;                  // lm_head argmax partial of this CTA
     int bi, nan0;
     int tok;
@@ -430,8 +454,8 @@ EMB_DEV void piece_mat(const PArgs &a, int l, int mat, const uint8_t **q, const 
     *cols = mat == W_O ? a.nh * a.hd : (mat == W_2 ? a.hidden : a.dim);
 }
 
-// thread 0: bulk-copy the piece at cursor c into `slot`, completing on `bar`
-// (slot layout: quant rows of A [of B], then A's [and B's] scale window)
+// bulk-copy the piece at cursor c into `slot`, completing on `bar` (slot
+// layout: quant rows of A [of B], then A's [and B's] scale window)
 EMB_DEV void issue_piece(const PArgs &a, const PieceTab &t, const Cursor &c, unsigned char *slot, uint64_t *bar) {
     const Piece &pc = t.p[t.first[c.s] + c.i];
     const uint8_t *q;
@@ -462,57 +486,56 @@ EMB_DEV void issue_piece(const PArgs &a, const PieceTab &t, const Cursor &c, uns
     }
 }
 
-// thread 0: issue the next piece of the sequence, if any is left
-EMB_DEV void ring_issue_next(const PArgs &a, const PieceTab &t, GShared &g, unsigned char *ring) {
-    if (g.ic.step >= a.n_steps) return;
-    const int slot = (int)(g.issued % P_NSLOT);
-    issue_piece(a, t, g.ic, ring + (size_t)slot * P_SLOT, &g.full[slot]);
-    g.issued++;
-    g.ic.i++;
-    if (g.ic.i >= t.n[g.ic.s]) cursor_next_stage(g.ic, t, a.L);
-}
-
-// Wait for the next piece to consume; returns its slot, or nullptr when the
-// wait gave up (error recorded) or another CTA reported an error.
-EMB_DEV const unsigned char *ring_acquire(const PArgs &a, GShared &g, unsigned char *ring) {
-    const unsigned k = g.consumed;
-    const int slot = (int)(k % P_NSLOT);
-    __shared__ int s_ok;
-    if (threadIdx.x == 0) {
-        int ok = 1;
-        uint32_t i = 0;
-        while (!mbar_try_wait(&g.full[slot], (k / P_NSLOT) & 1u)) {
-            if ((++i & 255u) == 0 && (ld_err(a.ctl + CTL_ERR) != 0 || i >= MBAR_TRIES)) {
-                if (i >= MBAR_TRIES) atomicExch(a.ctl + CTL_ERR, ERR_P_RING);
-                ok = 0;
-                break;
+// bounded wait on an mbarrier phase that gives up early when the error word is set
+EMB_DEV bool mbar_wait_err(uint64_t *bar, uint32_t parity, const PArgs &a, int code) {
+    uint32_t i = 0;
+    while (!mbar_try_wait(bar, parity)) {
+        if ((++i & 255u) == 0) {
+            if (ld_err(a.ctl + CTL_ERR) != 0) return false;
+            if (i >= MBAR_TRIES) {
+                atomicExch(a.ctl + CTL_ERR, code);
+                return false;
             }
         }
-        s_ok = ok;
     }
-    __syncthreads();
-    return s_ok ? ring + (size_t)slot * P_SLOT : nullptr;
+    return true;
 }
 
-// after every thread is done with the consumed slot: refill it
-EMB_DEV void ring_release(const PArgs &a, const PieceTab &t, GShared &g, unsigned char *ring) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        g.consumed++;
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        ring_issue_next(a, t, g, ring);
-    }
-}
-
-// On an error exit: wait (bounded) for the copies still in flight, so that no
-// bulk copy lands in shared memory after the CTA has left.
-EMB_DEV void ring_drain(GShared &g) {
-    if (threadIdx.x != 0) return;
-    for (unsigned k = g.consumed; k < g.issued; k++) {
+// The producer (lane 0 of warp 15): every piece of the launch in order, each
+// once its slot is released. On an error it stops issuing and waits (bounded)
+// for the copies it has in flight before the CTA leaves.
+EMB_DEV void ring_producer(const PArgs &a, const PieceTab &t, GShared &g, unsigned char *ring) {
+    Cursor c;
+    c.step = 0; c.l = 0; c.s = PS_QKV; c.i = 0;
+    if (t.n[PS_QKV] == 0) cursor_next_stage(c, t, a.L);
+    unsigned k = 0;
+    for (; c.step < a.n_steps; k++) {
         const int slot = (int)(k % P_NSLOT);
-        for (uint32_t i = 0; i < MBAR_TRIES; i++)
-            if (mbar_try_wait(&g.full[slot], (k / P_NSLOT) & 1u)) break;
+        if (k >= (unsigned)P_NSLOT && !mbar_wait_err(&g.empty[slot], ((k / P_NSLOT) - 1) & 1u, a, ERR_P_RING)) break;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue_piece(a, t, c, ring + (size_t)slot * P_SLOT, &g.full[slot]);
+        if (++c.i >= t.n[c.s]) cursor_next_stage(c, t, a.L);
     }
+    for (unsigned j = k > (unsigned)P_NSLOT ? k - P_NSLOT : 0; j < k; j++)
+        for (uint32_t i = 0; i < MBAR_TRIES; i++)
+            if (mbar_try_wait(&g.full[j % P_NSLOT], (j / P_NSLOT) & 1u)) break;
+}
+
+// Compute threads: wait for piece k (one lane per warp) and agree on the
+// outcome; false when a wait gave up or another CTA reported an error. The
+// piece is in slot k % P_NSLOT of the ring at the start of p_dyn.
+EMB_DEV bool ring_acquire(const PArgs &a, GShared &g, unsigned k) {
+    const int slot = (int)(k % P_NSLOT);
+    bool ok = true;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait_err(&g.full[slot], (k / P_NSLOT) & 1u, a, ERR_P_RING);
+    __syncwarp();
+    return !csync_or(!ok);
+}
+
+// a warp is past piece k's slot: its arrival on the slot's `empty` barrier
+EMB_DEV void ring_release(GShared &g, unsigned k) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&g.empty[k % P_NSLOT]);
 }
 
 // ---- activations in -----------------------------------------------------------------
@@ -523,7 +546,7 @@ EMB_DEV bool gather_x(const PArgs &a, float *xf, const unsigned long long *src, 
 #pragma unroll
     for (int j = 0; j < 4; j++)
         if ((int)threadIdx.x + j * PT < a.dim) xf[threadIdx.x + j * PT] = __uint_as_float(v[j]);
-    __syncthreads();
+    csync();
     return true;
 }
 
@@ -538,7 +561,7 @@ EMB_DEV bool gather_q8(const PArgs &a, int8_t *xq, float *xd, const unsigned lon
         if (i < n / 4) reinterpret_cast<uint32_t *>(xq)[i] = v[j];
         else if (i < nw) xd[i - n / 4] = __uint_as_float(v[j]);
     }
-    __syncthreads();
+    csync();
     return true;
 }
 
@@ -551,12 +574,12 @@ EMB_DEV void norm_quant(const PArgs &a, float *xf, float *sq, int8_t *xq, float 
     PDETAIL(6);
     cp_async_wait_1();
     for (int i = threadIdx.x; i < n; i += PT) sq[i] = fmul(xf[i], xf[i]);
-    __syncthreads();
+    csync();
     PDETAIL(7);
     const float sc = rms_scale(psum(sq, n), n, a.eps);
     PDETAIL(8);
     for (int i = threadIdx.x; i < n; i += PT) xf[i] = fmul(fmul(xf[i], sc), w_s[i]);
-    __syncthreads();
+    csync();
     PDETAIL(9);
     for (int base = 0; base < nb * 8; base += PT) {
         const int q8 = base + (int)threadIdx.x;
@@ -570,7 +593,7 @@ EMB_DEV void norm_quant(const PArgs &a, float *xf, float *sq, int8_t *xq, float 
             if (sub == 0) xd[b] = dq;
         }
     }
-    __syncthreads();
+    csync();
     PDETAIL(10);
 }
 
@@ -592,14 +615,70 @@ struct GViews {
 
 EMB_DEV bool am_better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
 
+// The Q8_0 terms of the rows of one piece, NSP 512-byte spans per row, fully
+// unrolled for the compiler: warp w takes rows w, w + 15, ... (RPW of them:
+// rows <= 15 RPW), lane l the 16 bytes [16 l, 16 l + 16) of each span, so all loads can be
+// in flight at once. x4 / dx: this lane's activation bytes and block scale per
+// span (read from the activation in shared memory, xq / xd). Row rr's weights
+// are at wq(rr), its fp16 scales at ws(rr), its terms go to P + rr * pstride.
+template <int NSP, int RPW, typename WQ, typename WS>
+EMB_DEV void dots_q8(const WQ &wq, const WS &ws, float *P, int pstride, int rows, int cols, const int8_t *xq,
+                     const float *xd) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int4 x4[NSP];
+    float dx[NSP];
+#pragma unroll
+    for (int sp = 0; sp < NSP; sp++) {
+        const int off = sp * 512 + lane * 16;
+        x4[sp] = off < cols ? *reinterpret_cast<const int4 *>(xq + off) : make_int4(0, 0, 0, 0);
+        dx[sp] = off < cols ? xd[off / 32] : 0.0f;
+    }
+    int acc[RPW][NSP];
+#pragma unroll
+    for (int k = 0; k < RPW; k++) {
+        const int rr = warp + k * PNW;
+        const uint8_t *w = wq(rr < rows ? rr : 0);
+#pragma unroll
+        for (int sp = 0; sp < NSP; sp++) {
+            const int off = sp * 512 + lane * 16;
+            int a = 0;
+            if (off < cols) {
+                const int4 w4 = *reinterpret_cast<const int4 *>(w + off);
+                a = __dp4a(w4.x, x4[sp].x, a); a = __dp4a(w4.y, x4[sp].y, a);
+                a = __dp4a(w4.z, x4[sp].z, a); a = __dp4a(w4.w, x4[sp].w, a);
+            }
+            acc[k][sp] = a;
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < RPW; k++) {
+        const int rr = warp + k * PNW;
+        const __half *s = ws(rr < rows ? rr : 0);
+#pragma unroll
+        for (int sp = 0; sp < NSP; sp++) {
+            const int off = sp * 512 + lane * 16;
+            const int a = acc[k][sp] + __shfl_xor_sync(0xffffffffu, acc[k][sp], 1);
+            if (rr < rows && off < cols && (lane & 1) == 0) {
+                const int b = off / 32;
+                P[rr * pstride + b] = fmul(fmul(__int2float_rn(a), __half2float(s[b])), dx[sp]);
+            }
+        }
+    }
+}
+
 // One stage of a GEMV CTA over its pieces of layer l. Per piece: each warp takes
-// rows (warp w: rows w, w+16, ...), its lanes the row's blocks, and forms the
-// terms ((float)acc * d_w) * d_x in shared memory; once every warp is done with
-// the slot it is refilled; then one lane per row adds the row's terms in block
-// order (ref src/kernels.c:152-164) and runs the stage's epilogue. The
-// activation (xq, xd) is in shared memory already.
+// rows (warp w: rows w, w+15, ...) and forms the terms ((float)acc * d_w) * d_x
+// of every block of the row in shared memory -- Q8_0 rows in 512-byte spans,
+// lane l reading bytes [16 l, 16 l + 16) of the span (contiguous across the
+// warp, so without bank conflicts) against the matching activation bytes held
+// in registers, the two lanes of a block joined by one shuffle (the int32 block
+// sum is exact in any order); Q4_0 rows a block per lane -- then releases the
+// slot; then one lane per row adds the row's terms in block order (ref
+// src/kernels.c:152-164) and runs the stage's epilogue. The activation (xq, xd)
+// is in shared memory already; kc counts the pieces consumed.
 template <int ST>
-EMB_DEV bool gemv_stage(const PArgs &a, const PieceTab &t, GShared &g, const GViews &v, int l, uint32_t tag) {
+EMB_DEV bool gemv_stage(const PArgs &a, const PieceTab &t, GShared &g, const GViews &v, int l, uint32_t tag,
+                        unsigned &kc) {
     constexpr int nsub = ST == PS_W13 ? 2 : 1;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const PLayer *Lp = p_layers + l;
@@ -608,8 +687,8 @@ EMB_DEV bool gemv_stage(const PArgs &a, const PieceTab &t, GShared &g, const GVi
     for (int i = 0; i < t.n[ST]; i++) {
         const Piece pc = t.p[t.first[ST] + i];
         if (ST == PS_QKV && i == 0) PDETAIL(0);
-        const unsigned char *slot = ring_acquire(a, g, v.ring);
-        if (!slot) return false;
+        if (!ring_acquire(a, g, kc)) return false;
+        const unsigned char *slot = p_dyn + (size_t)(kc % P_NSLOT) * P_SLOT;
         if (ST == PS_QKV && i == 0) PDETAIL(1);
         const uint8_t *q;
         const __half *s;
@@ -626,45 +705,78 @@ EMB_DEV bool gemv_stage(const PArgs &a, const PieceTab &t, GShared &g, const GVi
             scale_window(Lp->s[W_3], pc.row0, nr, nb, &src, &skip_b);
             sc_b = reinterpret_cast<const __half *>(slot + 2 * qbytes + sa_bytes + skip_b);
         }
-        // terms: warp-per-row, lane-per-block
         const int rows = nsub * nr;
-        for (int rr = warp; rr < rows; rr += PNW) {
-            const int sub = nsub == 2 && rr >= nr ? 1 : 0, r = rr - sub * nr;
-            const uint8_t *wq = slot + sub * qbytes + (size_t)r * qrb;
-            const __half *ws = (sub ? sc_b : sc_a) + r * nb;
-            float *pr = v.P + rr * pstride;
-            for (int b = lane; b < nb; b += 32) {
-                const int acc = dtype == EMBER_DT_Q8_0 ? dot_q8_block(wq + b * 32, v.xq + b * 32)
-                                                       : dot_q4_block(wq + b * 16, v.xq + b * 32);
-                pr[b] = fmul(fmul(__int2float_rn(acc), __half2float(ws[b])), v.xd[b]);
-            }
-        }
-        if (ST == PS_QKV && i == 0) PDETAIL(2);
 #ifdef EMBER_PROBES
-        if (ST == PS_QKV && i == 0 && p_detail) {
-            // the same dot loop once more, now warm, for the probe timeline
-            __syncthreads();
-            PDETAIL(11);
+        // profiling build: the first S1 piece's dot loop runs twice (the same
+        // instructions), to time it cold and warm
+        const int reps = (ST == PS_QKV && i == 0 && p_detail) ? 2 : 1;
+        for (int rep = 0; rep < reps; rep++) {
+        if (rep == 1) { csync(); PDETAIL(11); }
+#endif
+        if (dtype == EMBER_DT_Q8_0) {
+            const int nsp = (cols + 511) / 512;
+            auto wq = [&](int rr) {
+                const int sub = nsub == 2 && rr >= nr ? 1 : 0;
+                return slot + sub * qbytes + (size_t)(rr - sub * nr) * qrb;
+            };
+            auto wsf = [&](int rr) {
+                const int sub = nsub == 2 && rr >= nr ? 1 : 0;
+                return (sub ? sc_b : sc_a) + (rr - sub * nr) * nb;
+            };
+            if (nsp <= 2 && rows <= 3 * PNW) {
+                dots_q8<2, 3>(wq, wsf, v.P, pstride, rows, cols, v.xq, v.xd);
+            } else if (nsp <= 4 && rows <= 2 * PNW) {
+                dots_q8<4, 2>(wq, wsf, v.P, pstride, rows, cols, v.xq, v.xd);
+            } else if (nsp <= 6 && rows <= PNW) {
+                dots_q8<6, 1>(wq, wsf, v.P, pstride, rows, cols, v.xq, v.xd);
+            } else {
+                // wider rows or taller pieces: span by span, a row at a time
+                for (int rr = warp; rr < rows; rr += PNW) {
+                    const uint8_t *w = wq(rr);
+                    const __half *sc = wsf(rr);
+                    for (int sp = 0; sp < nsp; sp++) {
+                        const int off = sp * 512 + lane * 16;
+                        const int4 x4 = off < cols ? *reinterpret_cast<const int4 *>(v.xq + off) : make_int4(0, 0, 0, 0);
+                        int acc = 0;
+                        if (off < cols) {
+                            const int4 w4 = *reinterpret_cast<const int4 *>(w + off);
+                            acc = __dp4a(w4.x, x4.x, acc); acc = __dp4a(w4.y, x4.y, acc);
+                            acc = __dp4a(w4.z, x4.z, acc); acc = __dp4a(w4.w, x4.w, acc);
+                        }
+                        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+                        if (off < cols && (lane & 1) == 0) {
+                            const int bk = off / 32;
+                            v.P[rr * pstride + bk] = fmul(fmul(__int2float_rn(acc), __half2float(sc[bk])), v.xd[bk]);
+                        }
+                    }
+                }
+            }
+        } else {
             for (int rr = warp; rr < rows; rr += PNW) {
                 const int sub = nsub == 2 && rr >= nr ? 1 : 0, r = rr - sub * nr;
                 const uint8_t *wq = slot + sub * qbytes + (size_t)r * qrb;
                 const __half *ws = (sub ? sc_b : sc_a) + r * nb;
                 float *pr = v.P + rr * pstride;
                 for (int b = lane; b < nb; b += 32) {
-                    const int acc = dtype == EMBER_DT_Q8_0 ? dot_q8_block(wq + b * 32, v.xq + b * 32)
-                                                           : dot_q4_block(wq + b * 16, v.xq + b * 32);
+                    const int acc = dot_q4_block(wq + b * 16, v.xq + b * 32);
                     pr[b] = fmul(fmul(__int2float_rn(acc), __half2float(ws[b])), v.xd[b]);
                 }
             }
-            __syncthreads();
-            PDETAIL(12);
         }
+#ifdef EMBER_PROBES
+        if (rep == 0) { csync(); if (ST == PS_QKV && i == 0) PDETAIL(2); }
+        }
+        if (reps == 2) { csync(); PDETAIL(12); }
+#else
+        if (ST == PS_QKV && i == 0) PDETAIL(2);
 #endif
-        ring_release(a, t, g, v.ring);   // every warp is past the slot
+        ring_release(g, kc);
+        kc++;
+        csync();
         if (ST == PS_QKV && i == 0) PDETAIL(3);
-        // chains and epilogue: row rr = warp + 16 * lane on lanes 0..3
+        // chains and epilogue: row rr = warp + 15 * lane on lanes 0..4
         const int rr = warp + PNW * lane;
-        if (lane < 4 && rr < rows) {
+        if (lane < 5 && rr < rows) {
             const float y = pchain(v.P + rr * pstride, nb);
             if (ST == PS_QKV) {
                 float o = y;
@@ -687,7 +799,7 @@ EMB_DEV bool gemv_stage(const PArgs &a, const PieceTab &t, GShared &g, const GVi
         if (ST == PS_QKV && i == 0) PDETAIL(4);
         if (ST == PS_W13) {
             // h = SiLU(g) * u = g / (1 + expf(-g)) * u (ref src/model.c:403-406)
-            __syncthreads();
+            csync();
             const int in_blk = pc.out0 & 31;
             if (tid < nr) {
                 const float gv = v.rowsum[tid], uv = v.rowsum[nr + tid];
@@ -696,7 +808,7 @@ EMB_DEV bool gemv_stage(const PArgs &a, const PieceTab &t, GShared &g, const GVi
             }
             if (in_blk + nr == 32) {
                 // the block of h is complete: its Q8 quantization for w2, published
-                __syncthreads();
+                csync();
                 if (tid < 32) {
                     float dq;
                     const int8_t qv = quant_lane(v.hbuf[tid], &dq);
@@ -709,6 +821,7 @@ EMB_DEV bool gemv_stage(const PArgs &a, const PieceTab &t, GShared &g, const GVi
                 }
             }
         }
+        csync();   // P is written again by the next piece
     }
     if (ST == PS_HEAD) {
         // this CTA's first maximum over all its rows: lanes, then warps
@@ -721,7 +834,7 @@ EMB_DEV bool gemv_stage(const PArgs &a, const PieceTab &t, GShared &g, const GVi
         __shared__ float h_v[PNW];
         __shared__ int h_i[PNW];
         if (lane == 0) { h_v[warp] = hb_v; h_i[warp] = hb_i; }
-        __syncthreads();
+        csync();
         if (warp == 0) {
             float bv = lane < PNW ? h_v[lane] : -INFINITY;
             int bi = lane < PNW ? h_i[lane] : 0x7FFFFFFF;
@@ -733,8 +846,8 @@ EMB_DEV bool gemv_stage(const PArgs &a, const PieceTab &t, GShared &g, const GVi
             }
             if (lane == 0 && am_better(bv, bi, g.bv, g.bi)) { g.bv = bv; g.bi = bi; }
         }
+        csync();
     }
-    __syncthreads();
     return true;
 }
 
@@ -804,7 +917,7 @@ EMB_DEV bool attn_wait_v(const PArgs &a, AShared &sh, int i) {
         }
         s_ok = ok;
     }
-    __syncthreads();
+    csync();
     return s_ok != 0;
 }
 
@@ -836,19 +949,19 @@ EMB_DEV bool attn_stage(const PArgs &a, AShared &sh, unsigned char *smem, const 
         if (tid < hd) sh.qs[tid] = __uint_as_float(val);
         else if (tid < 2 * hd) sh.ks[tid - hd] = __uint_as_float(val);
         else if (tid < 3 * hd) sh.vs[tid - 2 * hd] = __uint_as_float(val);
-        __syncthreads();
+        csync();
     }
     PPROBE(role, l, 1);
     if (a.qk_norm && Lp->q_norm) {
         // per-head RMSNorm of q and k (ref src/model.c:386-389), two chains on two warps
         if (tid == 0) sh.s_q = rms_scale(chain_sumsq(sh.qs, hd), hd, a.eps);
         else if (tid == 32) sh.s_k = rms_scale(chain_sumsq(sh.ks, hd), hd, a.eps);
-        __syncthreads();
+        csync();
         if (tid < hd) {
             sh.qs[tid] = fmul(fmul(sh.qs[tid], sh.s_q), sh.qn[tid]);
             sh.ks[tid] = fmul(fmul(sh.ks[tid], sh.s_k), sh.kn[tid]);
         }
-        __syncthreads();
+        csync();
     }
     // RoPE (ref src/model.c:66-80) with the host-built cos/sin table
     if (tid < hd / 2) {
@@ -861,7 +974,7 @@ EMB_DEV bool attn_stage(const PArgs &a, AShared &sh, unsigned char *smem, const 
         sh.ks[ia] = fsub(fmul(v0, cs.x), fmul(v1, cs.y));
         sh.ks[ib] = fadd(fmul(v0, cs.y), fmul(v1, cs.x));
     }
-    __syncthreads();
+    csync();
     // KV store (ref src/model.c:39-48): attention reads the stored (rounded)
     // values, including at t == pos; the first query head of each kv head writes
     // the cache (and fences after publishing its output, before anything of a
@@ -877,7 +990,7 @@ EMB_DEV bool attn_stage(const PArgs &a, AShared &sh, unsigned char *smem, const 
             vt[(size_t)pos * hd + tid] = vq;
         }
     }
-    __syncthreads();
+    csync();
     PPROBE(role, l, 2);
     // scores: sc = sum_i q_i*k_i in index order, then * (1/sqrt(hd))
     const float inv_sqrt = fdiv(1.0f, fsqrt((float)hd));
@@ -900,7 +1013,7 @@ EMB_DEV bool attn_stage(const PArgs &a, AShared &sh, unsigned char *smem, const 
     // zeros after the last score, up to the padded length of the denominator
     const int npad = (pos + 1 + 63) / 64 * 64;
     for (int t = pos + 1 + tid; t < npad; t += PT) att[t] = 0.0f;
-    __syncthreads();
+    csync();
     PPROBE(role, l, 3);
     // the keys are done: the values past the value region stream into their space
     if (tid == 0 && pos > a.vcap0) {
@@ -915,23 +1028,23 @@ EMB_DEV bool attn_stage(const PArgs &a, AShared &sh, unsigned char *smem, const 
     for (int t = tid; t <= pos; t += PT) tmax = fmaxf(tmax, att[t]);
     tmax = warp_max(tmax);
     if (lane == 0) sh.red[warp] = tmax;
-    __syncthreads();
+    csync();
     if (warp == 0) {
         const float m = warp_max(lane < PNW ? sh.red[lane] : -INFINITY);
         if (lane == 0) sh.s_max = m;
     }
-    __syncthreads();
+    csync();
     const float mx = sh.s_max;
     for (int t = tid; t <= pos; t += PT) att[t] = expf_exact(a.ex, tab, fsub(att[t], mx));
-    __syncthreads();
+    csync();
     // the denominator: the reference's sequential sum over t = 0..pos (the zero
     // padding adds nothing)
     const float den = psum(att, npad);
     if (tid == 0) sh.s_inv = fdiv(1.0f, den);
-    __syncthreads();
+    csync();
     const float inv = sh.s_inv;
     for (int t = tid; t <= pos; t += PT) att[t] = fmul(att[t], inv);
-    __syncthreads();
+    csync();
     PPROBE(role, l, 4);
     // out_i = sum_t w_t * v_t,i, sequential over t (ref src/model.c:252-256)
     if (!attn_wait_v(a, sh, 0)) return false;
@@ -982,7 +1095,7 @@ EMB_DEV bool attn_stage(const PArgs &a, AShared &sh, unsigned char *smem, const 
     // the cache entry written above, ordered before every later hand-off of this
     // CTA (its readers come a step later, behind several of them)
     if (tid < hd && h % kv_mul == 0) __threadfence();
-    __syncthreads();
+    csync();
     return true;
 }
 
@@ -1044,7 +1157,7 @@ EMB_DEV void embed_row(const PArgs &a, int tok, float *xf) {
     const int8_t *row = reinterpret_cast<const int8_t *>(a.emb_q) + (size_t)tok * a.dim;
     const __half *sc = a.emb_s + (size_t)tok * (a.dim / 32);
     for (int i = threadIdx.x; i < a.dim; i += PT) xf[i] = fmul((float)row[i], __half2float(sc[i / 32]));
-    __syncthreads();
+    csync();
 }
 
 EMB_DEV bool gemv_cta(const PArgs &a, unsigned char *smem, double *tab, int gi, int G) {
@@ -1052,17 +1165,17 @@ EMB_DEV bool gemv_cta(const PArgs &a, unsigned char *smem, double *tab, int gi, 
     __shared__ __align__(8) GShared g;
     const int tid = threadIdx.x, L = a.L, qd = a.nh * a.hd;
     GViews v;
-    v.ring = smem;
-    v.xf = reinterpret_cast<float *>(smem + a.g_xf);
-    v.sq = reinterpret_cast<float *>(smem + a.g_sq);
-    v.xq = reinterpret_cast<int8_t *>(smem + a.g_xq);
-    v.xd = reinterpret_cast<float *>(smem + a.g_xd);
-    v.P = reinterpret_cast<float *>(smem + a.g_p);
-    v.rowsum = reinterpret_cast<float *>(smem + a.g_rowsum);
-    v.hbuf = reinterpret_cast<float *>(smem + a.g_h);
-    v.xown = reinterpret_cast<float *>(smem + a.g_xown);
-    v.nw = reinterpret_cast<float *>(smem + a.g_nw);
-    v.bias = reinterpret_cast<float *>(smem + a.g_bias);
+    v.ring = p_dyn;
+    v.xf = reinterpret_cast<float *>(p_dyn + a.g_xf);
+    v.sq = reinterpret_cast<float *>(p_dyn + a.g_sq);
+    v.xq = reinterpret_cast<int8_t *>(p_dyn + a.g_xq);
+    v.xd = reinterpret_cast<float *>(p_dyn + a.g_xd);
+    v.P = reinterpret_cast<float *>(p_dyn + a.g_p);
+    v.rowsum = reinterpret_cast<float *>(p_dyn + a.g_rowsum);
+    v.hbuf = reinterpret_cast<float *>(p_dyn + a.g_h);
+    v.xown = reinterpret_cast<float *>(p_dyn + a.g_xown);
+    v.nw = reinterpret_cast<float *>(p_dyn + a.g_nw);
+    v.bias = reinterpret_cast<float *>(p_dyn + a.g_bias);
     v.tab = tab;
     v.own0 = (int)((long)gi * a.dim / G);
     v.own1 = (int)((long)(gi + 1) * a.dim / G);
@@ -1100,17 +1213,21 @@ EMB_DEV bool gemv_cta(const PArgs &a, unsigned char *smem, double *tab, int gi, 
         }
         cp_async_commit();
     };
-    issue_norms(0);
     if (tid == 0) {
         build_pieces(a, t, gi, G);
-        for (int s = 0; s < P_NSLOT; s++) mbar_init(&g.full[s], 1);
+        for (int s = 0; s < P_NSLOT; s++) {
+            mbar_init(&g.full[s], 1);
+            mbar_init(&g.empty[s], PNW);
+        }
         fence_mbar_init();
-        g.issued = g.consumed = 0;
-        g.ic.step = 0; g.ic.l = 0; g.ic.s = PS_QKV; g.ic.i = 0;
-        if (t.n[PS_QKV] == 0) cursor_next_stage(g.ic, t, L);
-        for (int k = 0; k < P_NSLOT; k++) ring_issue_next(a, t, g, v.ring);
     }
-    __syncthreads();
+    __syncthreads();   // all 544 threads: the piece table and barriers are ready
+    if (tid >= PT) {   // the producer warp
+        if (tid == PT) ring_producer(a, t, g, v.ring);
+        return true;
+    }
+    issue_norms(0);
+    unsigned kc = 0;   // pieces consumed
     bool ok = true;
     const int role = gi == 0 ? 0 : (gi == G - 1 ? 1 : -1);
     (void)role;
@@ -1132,30 +1249,30 @@ EMB_DEV bool gemv_cta(const PArgs &a, unsigned char *smem, double *tab, int gi, 
             PPROBE(role, l, 1);
 #ifdef EMBER_PROBES
             if (tid == 0) p_detail = probe_on && role == 0 && l == 1;
-            __syncthreads();
+            csync();
 #endif
             for (int r = v.own0 + tid; r < v.own1; r += PT) v.xown[r - v.own0] = v.xf[r];
             norm_quant(a, v.xf, v.sq, v.xq, v.xd, nw);
             PPROBE(role, l, 2);
-            ok = gemv_stage<PS_QKV>(a, t, g, v, l, TL + TG_QKV);
+            ok = gemv_stage<PS_QKV>(a, t, g, v, l, TL + TG_QKV, kc);
             PPROBE(role, l, 3);
 #ifdef EMBER_PROBES
             if (tid == 0) p_detail = 0;
 #endif
             ok = ok && gather_q8(a, v.xq, v.xd, a.w_o, qd, TL + TG_O);
             PPROBE(role, l, 4);
-            ok = ok && gemv_stage<PS_WO>(a, t, g, v, l, TL + TG_XA);
+            ok = ok && gemv_stage<PS_WO>(a, t, g, v, l, TL + TG_XA, kc);
             PPROBE(role, l, 5);
             ok = ok && gather_x(a, v.xf, a.w_x, TL + TG_XA);
             PPROBE(role, l, 6);
             if (!ok) break;
             norm_quant(a, v.xf, v.sq, v.xq, v.xd, nw + a.dim);
             PPROBE(role, l, 7);
-            ok = gemv_stage<PS_W13>(a, t, g, v, l, TL + TG_H);
+            ok = gemv_stage<PS_W13>(a, t, g, v, l, TL + TG_H, kc);
             PPROBE(role, l, 8);
             ok = ok && gather_q8(a, v.xq, v.xd, a.w_h, a.hidden, TL + TG_H);
             PPROBE(role, l, 9);
-            ok = ok && gemv_stage<PS_W2>(a, t, g, v, l, TL + TG_XB);
+            ok = ok && gemv_stage<PS_W2>(a, t, g, v, l, TL + TG_XB, kc);
             PPROBE(role, l, 10);
         }
         if (!ok) break;
@@ -1168,9 +1285,9 @@ EMB_DEV bool gemv_cta(const PArgs &a, unsigned char *smem, double *tab, int gi, 
         PPROBE(role, L, 1);
         norm_quant(a, v.xf, v.sq, v.xq, v.xd, v.nw + (grp & 1) * 2 * a.dim);
         if (tid == 0) { g.bv = -INFINITY; g.bi = 0x7FFFFFFF; g.nan0 = 0; }
-        __syncthreads();
+        csync();
         PPROBE(role, L, 2);
-        if (!gemv_stage<PS_HEAD>(a, t, g, v, 0, 0)) { ok = false; break; }
+        if (!gemv_stage<PS_HEAD>(a, t, g, v, 0, 0, kc)) { ok = false; break; }
         PPROBE(role, L, 3);
         if (step + 1 == a.n_steps && a.out_tokens == nullptr) break;   // forward: no pick
         if (tid == 0) {
@@ -1184,7 +1301,7 @@ EMB_DEV bool gemv_cta(const PArgs &a, unsigned char *smem, double *tab, int gi, 
             if (!tw_wait<1>(w, a.w_am, 2 * G, TH, a)) { ok = false; break; }
             float *pv = v.P;
             if (tid < 2 * G) pv[tid] = __uint_as_float(w[0]);
-            __syncthreads();
+            csync();
             if (tid < 32) {
                 float bv = -INFINITY;
                 int bi = 0x7FFFFFFF, nan0 = 0;
@@ -1202,15 +1319,14 @@ EMB_DEV bool gemv_cta(const PArgs &a, unsigned char *smem, double *tab, int gi, 
                 }
                 if (tid == 0) g.tok = (nan0 || bi == 0x7FFFFFFF) ? 0 : bi;
             }
-            __syncthreads();
+            csync();
             tok = g.tok;
             if (gi == 0 && tid == 0 && a.out_tokens) a.out_tokens[nout0 + step] = tok;
             PPROBE(role, L, 4);
         }
     }
     if (!ok) {
-        ring_drain(g);
-        cp_async_wait_all();
+        cp_async_wait_all();   // (the producer waits for the weight copies it issued)
         return false;
     }
     cp_async_wait_all();
@@ -1227,6 +1343,7 @@ template <typename T>
 EMB_DEV bool attn_cta(const PArgs &a, unsigned char *smem, const double *tab) {
     __shared__ __align__(16) AShared sh;
     const int tid = threadIdx.x, L = a.L;
+    if (tid >= PT) return true;   // attention needs no producer warp
     const uint32_t T0 = (uint32_t)a.ctl[CTL_TAG];
     const int pos0 = a.ctl[CTL_POS];
     if (tid == 0) {
@@ -1236,7 +1353,7 @@ EMB_DEV bool attn_cta(const PArgs &a, unsigned char *smem, const double *tab) {
         sh.vph[0] = sh.vph[1] = 0;
         sh.pending[0] = sh.pending[1] = 0;
     }
-    __syncthreads();
+    csync();
     attn_prefetch<T>(a, sh, smem, 0, pos0);
     bool ok = true;
     const int role = blockIdx.x == 0 ? 2 : ((int)blockIdx.x == a.n_att - 1 ? 3 : -1);
@@ -1261,7 +1378,7 @@ EMB_DEV bool attn_cta(const PArgs &a, unsigned char *smem, const double *tab) {
                 if (sh.pending[i])
                     for (uint32_t k = 0; k < MBAR_TRIES; k++)
                         if (mbar_try_wait(&sh.vbar[i], sh.vph[i])) break;
-        __syncthreads();
+        csync();
     }
     return ok;
 }
@@ -1269,11 +1386,11 @@ EMB_DEV bool attn_cta(const PArgs &a, unsigned char *smem, const double *tab) {
 // One launch: n_steps token steps (greedy picks between them when out_tokens is
 // set; a single forward step otherwise). Cooperative launch: every CTA resident.
 template <typename T>
-__global__ void __launch_bounds__(PT, 1) ember_persist_kernel(const __grid_constant__ PArgs a) {
-    extern __shared__ __align__(128) unsigned char smem[];
+__global__ void __launch_bounds__(PTT, 1) ember_persist_kernel(const __grid_constant__ PArgs a) {
+    unsigned char *const smem = p_dyn;
     __shared__ double tab[64];
     expf_table_load(tab, a.ex);
-    for (int i = threadIdx.x; i < a.L * (int)(sizeof(PLayer) / 8); i += PT)
+    for (int i = threadIdx.x; i < a.L * (int)(sizeof(PLayer) / 8); i += PTT)
         reinterpret_cast<unsigned long long *>(p_layers)[i] = reinterpret_cast<const unsigned long long *>(a.layers)[i];
     __syncthreads();
     if ((int)blockIdx.x < a.n_att) attn_cta<T>(a, smem, tab);

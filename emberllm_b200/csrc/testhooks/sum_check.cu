@@ -9,7 +9,7 @@
 namespace emb {
 
 __global__ void __launch_bounds__(256) split_sum_check_kernel(const float *v, int n, float *out, int *hit) {
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(128) unsigned char smem[];
     float *t = reinterpret_cast<float *>(smem);
     const float *x = v + (size_t)blockIdx.x * n;
     for (int i = threadIdx.x; i < n; i += 256) t[i] = x[i];
@@ -24,7 +24,7 @@ __global__ void __launch_bounds__(256) split_sum_check_kernel(const float *v, in
 
 // the persistent step's 512-thread variant (psum, csrc/cuda/persist.cuh)
 __global__ void __launch_bounds__(PT) psum_check_kernel(const float *v, int n, float *out) {
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(128) unsigned char smem[];
     float *t = reinterpret_cast<float *>(smem);
     const float *x = v + (size_t)blockIdx.x * n;
     for (int i = threadIdx.x; i < n; i += PT) t[i] = x[i];

@@ -71,9 +71,11 @@ def _prompt(vocab, n, seed=1):
     return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, n)]
 
 
-def test_qwen3_bench_workload_128_greedy(prod, orc):
+@pytest.mark.parametrize("persist", ["0", "1"])
+def test_qwen3_bench_workload_128_greedy(prod, orc, persist, monkeypatch):
     """configs[3] exactly as bench.py times it: depth 128, 128 greedy tokens,
-    context depth + tokens + 8 (the single-kernel decode attention)"""
+    context depth + tokens + 8, on the graph step and on the persistent kernel"""
+    monkeypatch.setenv("EMBER_PERSIST", persist)
     depth, ntok = 128, 128
     ctx = depth + ntok + 8
     prompt = _prompt(151936, depth)
@@ -110,11 +112,12 @@ def test_smollm2_q4_prefill512_greedy256(prod, orc):
 @pytest.mark.parametrize("name,ctx,want", [("qwen3-0.6b", 264, 1), ("qwen2.5-0.5b", 648, 1),
                                            ("smollm2-135m", 776, 1), ("stories110m", 264, 1),
                                            ("qwen3-0.6b", 1048, 0)])
-def test_which_decode_path_serves_each_config(prod, name, ctx, want):
-    """the BASELINE decode configurations run as the persistent kernel (the bench
-    workload included); contexts whose keys exceed shared memory keep the graph
-    step with the split attention"""
+def test_which_decode_path_serves_each_config(prod, name, ctx, want, monkeypatch):
+    """with the persistent step requested (EMBER_PERSIST=1), the BASELINE decode
+    configurations run as the persistent kernel (the bench workload included);
+    contexts whose keys exceed shared memory keep the graph step"""
     from .test_gpu_parity import is_persistent
+    monkeypatch.setenv("EMBER_PERSIST", "1")
     a = prod.session(synth.ensure_model(name), ctx, 0)
     got, why = is_persistent(prod.lib, a)
     a.close()
