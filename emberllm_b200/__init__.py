@@ -14,7 +14,7 @@ import ctypes
 from . import _lib as _libmod
 from ._lib import EmberHeader, cuda_available, load
 
-__all__ = ["Ember", "EmberHeader", "cuda_available", "load"]
+__all__ = ["Ember", "EmberBatch", "Sampler", "EmberHeader", "cuda_available", "load"]
 
 
 class Ember:
@@ -57,6 +57,13 @@ class Ember:
         if max_tokens <= 1:
             return [best][:max_tokens]
         return [best] + self.greedy(best, len(prompt_ids), max_tokens - 1)
+
+    def sample(self, sampler):
+        """Draw the next token from the logits of the last forward / prefill on
+        the device with ``sampler``'s settings, random stream and history, then
+        record it in the history, as the reference's ember_sample does
+        (src/sample.c:120-175)."""
+        return sampler.sample_device(self)
 
     # -- lifetime ----------------------------------------------------------
     def close(self):
@@ -115,3 +122,54 @@ class EmberBatch:
             self.lib.ember_batch_free(self.b)
             self.b = None
 
+
+
+class Sampler:
+    """The reference's EmberSampler (src/ember.h:141-155, src/sample.c:17-67) on
+    the host: settings, the xorshift64* state and the ring of recent tokens.
+    Drawing runs on the device (``Ember.sample``); the history ring and the
+    random stream advance exactly as the reference's."""
+
+    def __init__(self, temperature=0.0, top_p=1.0, top_k=0, seed=0):
+        self.temperature, self.top_p, self.top_k = float(temperature), float(top_p), int(top_k)
+        self.min_p, self.repeat_penalty = 0.0, 1.0
+        self.presence_penalty = self.frequency_penalty = 0.0
+        self.repeat_last_n = 0
+        self.rng_state = ctypes.c_uint64(seed if seed else 0x9E3779B97F4A7C15)
+        self.history = None
+        self.hist_len = self.hist_pos = 0
+
+    def set_penalties(self, repeat_penalty=1.0, repeat_last_n=0, presence_penalty=0.0, frequency_penalty=0.0,
+                      min_p=0.0):
+        """as ember_sampler_set_penalties: a history of repeat_last_n tokens only
+        when some penalty is active; the history restarts empty"""
+        self.repeat_penalty, self.repeat_last_n = float(repeat_penalty), int(repeat_last_n)
+        self.presence_penalty, self.frequency_penalty = float(presence_penalty), float(frequency_penalty)
+        self.min_p = float(min_p)
+        need = self.repeat_last_n > 0 and (self.repeat_penalty != 1.0 or self.presence_penalty != 0.0
+                                           or self.frequency_penalty != 0.0)
+        self.history = (ctypes.c_int * self.repeat_last_n)() if need else None
+        self.hist_len = self.hist_pos = 0
+
+    def accept(self, token):
+        """record an emitted token in the ring (ember_sampler_accept)"""
+        if self.history is None:
+            return
+        self.history[self.hist_pos] = int(token)
+        self.hist_pos = (self.hist_pos + 1) % len(self.history)
+        if self.hist_len < len(self.history):
+            self.hist_len += 1
+
+    def reset(self):
+        self.hist_len = self.hist_pos = 0
+
+    def params(self):
+        return _libmod.EmberSampleParams(self.temperature, self.top_p, self.top_k, self.min_p,
+                                         self.repeat_penalty, self.presence_penalty, self.frequency_penalty)
+
+    def sample_device(self, ember):
+        p = self.params()
+        tok = ember.lib.ember_sample_device(ember.st, ctypes.byref(p), ctypes.byref(self.rng_state),
+                                            self.history if self.hist_len else None, self.hist_len)
+        self.accept(tok)
+        return tok

@@ -43,6 +43,14 @@ class EmberHeader(ctypes.Structure):
 
 assert ctypes.sizeof(EmberHeader) == 256
 
+
+class EmberSampleParams(ctypes.Structure):
+    """The sampler settings of ember_sample_device (include/ember_cuda.h)."""
+
+    _fields_ = [("temperature", ctypes.c_float), ("top_p", ctypes.c_float), ("top_k", ctypes.c_int32),
+                ("min_p", ctypes.c_float), ("repeat_penalty", ctypes.c_float),
+                ("presence_penalty", ctypes.c_float), ("frequency_penalty", ctypes.c_float)]
+
 # every symbol the headers declare, grouped by header (tests check the exports)
 PUBLIC_SYMBOLS = [
     "ember_model_load", "ember_model_free", "ember_model_header", "ember_model_tensor",
@@ -64,7 +72,8 @@ CUDA_SYMBOLS = [
     "ember_cuda_available", "ember_cuda_profile_step", "ember_cuda_mark", "ember_cuda_elapsed_ms",
     "ember_cuda_time_kernel", "ember_cuda_argmax_static", "ember_host_expf_params",
     "ember_host_expf_emulated",
-    "ember_host_rope_table", "ember_forward_greedy", "ember_state_cuda",
+    "ember_host_rope_table", "ember_forward_greedy", "ember_state_cuda", "ember_cuda_sample",
+    "ember_sample_device",
     "ember_cuda_batch_new", "ember_cuda_batch_free", "ember_cuda_batch_prefill", "ember_cuda_batch_greedy",
     "ember_cuda_batch_stream", "ember_batch_new", "ember_batch_free", "ember_batch_prefill",
     "ember_batch_greedy",
@@ -135,6 +144,12 @@ def load(path=None):
     lib.ember_cuda_state_launches_per_step.argtypes = [_P]
     lib.ember_cuda_state_persistent.restype = ctypes.c_int
     lib.ember_cuda_state_persistent.argtypes = [_P, ctypes.POINTER(ctypes.c_char_p)]
+    lib.ember_cuda_sample.restype = ctypes.c_int
+    lib.ember_cuda_sample.argtypes = [_P, ctypes.POINTER(EmberSampleParams), ctypes.c_float, _IP, ctypes.c_int,
+                                      ctypes.POINTER(ctypes.c_int)]
+    lib.ember_sample_device.restype = ctypes.c_int
+    lib.ember_sample_device.argtypes = [_P, ctypes.POINTER(EmberSampleParams), ctypes.POINTER(ctypes.c_uint64),
+                                        _IP, ctypes.c_int]
     lib.ember_cuda_greedy.restype = ctypes.c_int
     lib.ember_cuda_greedy.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _IP, _FP]
     lib.ember_cuda_error.restype = ctypes.c_char_p

@@ -220,6 +220,7 @@ extern "C" uint64_t ember_cuda_model_bytes(const EmberCudaModel *m) { return m ?
 static void state_release(EmberCudaState *s) {
     pf_state_release(s);
     persist_release(s);
+    sample_release(s);
     if (s->g_fwd) cudaGraphExecDestroy(s->g_fwd);
     if (s->g_greedy) cudaGraphExecDestroy(s->g_greedy);
     if (s->g_prefill) cudaGraphExecDestroy(s->g_prefill);

@@ -44,6 +44,7 @@ namespace emb {
 struct PfModel;   // batched-prefill weight packs (prefill.cu), built on first use
 struct PfState;   // batched-prefill activations (prefill.cu), built on first use
 struct PState;    // the persistent token step's plan and hand-off buffers (persist.cu)
+struct SampleBufs;  // device sampling scratch (sample.cu), built on first use
 }  // namespace emb
 
 struct EmberCudaModel {
@@ -101,6 +102,7 @@ struct EmberCudaState {
     int launches_per_step = 0;
     emb::PfState *pf = nullptr;
     emb::PState *ps = nullptr;             // set when the persistent token step serves this state
+    emb::SampleBufs *sb = nullptr;         // device sampling scratch
 };
 
 static inline int salloc(EmberCudaState *s, void **p, size_t n) {
@@ -127,6 +129,11 @@ void persist_release(EmberCudaState *s);
 // enqueue n_steps token steps from ctl's token and position on s->stream;
 // greedy: pick between steps and write the picks to s->out_tokens
 int persist_run(EmberCudaState *s, int n_steps, int greedy);
+}  // namespace emb
+
+// ---- device sampling (sample.cu) ----
+namespace emb {
+void sample_release(EmberCudaState *s);
 }  // namespace emb
 
 // ---- batched prefill (prefill.cu) ----

@@ -215,6 +215,31 @@ float *ember_forward_greedy(EmberModel *m, EmberState *s, int tok, int pos, int 
 
 EmberCudaState *ember_state_cuda(EmberState *s) { return s->dev; }
 
+/* ---- sampling on the device (extension) ----
+ * The sampler's random stream is xorshift64* (Vigna's generator: shifts 12, 25,
+ * 27, multiplier 0x2545F4914F6CDD1D, high 32 bits), mapped to [0, 1) as the top 24
+ * bits / 2^24, the draw the reference's sampler makes (ref src/sample.c:98-105);
+ * its steps must match for a seed to reproduce the reference's tokens. */
+static uint32_t xs64_u32(uint64_t *state) {
+    uint64_t x = *state;
+    x ^= x >> 12;
+    x ^= x << 25;
+    x ^= x >> 27;
+    *state = x;
+    return (uint32_t)((x * 0x2545F4914F6CDD1DULL) >> 32);
+}
+
+int ember_sample_device(EmberState *s, const EmberSampleParams *p, uint64_t *rng_state, const int *history,
+                        int hist_len) {
+    if (!p || !rng_state) ember_die("ember_sample_device: null sampler settings");
+    /* the reference draws once, after the softmax, only when temperature > 0 */
+    float u = 0.0f;
+    if (p->temperature > 0.0f) u = (float)(xs64_u32(rng_state) >> 8) / 16777216.0f;
+    int tok = 0;
+    cuda_check(ember_cuda_sample(s->dev, p, u, history, history ? hist_len : 0, &tok), "sample");
+    return tok;
+}
+
 /* ---- batched greedy decode of independent streams (extension) ---- */
 struct EmberBatch {
     EmberCudaBatch *dev;

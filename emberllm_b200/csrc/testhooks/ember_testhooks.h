@@ -20,6 +20,11 @@ int ember_cuda_split_sum_batch(const float *host_terms, int n, int count, float 
  * `count` vectors of n non-negative terms (n a multiple of 16, <= 32768). */
 int ember_cuda_psum_batch(const float *host_terms, int n, int count, float *host_out);
 
+/* Copy `bytes` from host memory to a device pointer that the product library
+ * allocated (e.g. a state's logits), on the device that owns it: tests plant
+ * inputs for a kernel that reads state buffers. */
+int ember_testhook_copy_to_device(void *dev_dst, const void *host_src, unsigned long long bytes);
+
 #ifdef __cplusplus
 }
 #endif

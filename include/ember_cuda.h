@@ -160,6 +160,26 @@ int  ember_cuda_batch_greedy(EmberCudaBatch *b, const int *toks, const int *pos,
                              float *host_logits);
 void *ember_cuda_batch_stream(EmberCudaBatch *b);                /* cudaStream_t */
 
+/* ---- sampling on the device ----
+ * The settings of the reference's sampler (EmberSampler, ref src/ember.h:141-155)
+ * that decide a draw: temperature, top_p, top_k, min_p and the three penalties. */
+typedef struct {
+    float   temperature, top_p;
+    int32_t top_k;
+    float   min_p, repeat_penalty, presence_penalty, frequency_penalty;
+} EmberSampleParams;
+
+/* The reference's ember_sample (src/sample.c:120-175) over the state's last
+ * logits, on the device: penalties over hist[0..hist_len) (the sampler's history
+ * array and length, in array order as the reference scans it), then greedy
+ * (temperature <= 0) or temperature, softmax, stable descending order, top_k,
+ * min_p, top_p and the draw r = u * cutoff, with u the reference's rng_f32 draw
+ * (computed by the caller; ember_sample_device does it). The token to
+ * *out_token; the state's logits are left as they were. No counterpart in the
+ * reference (which samples on the host). */
+int  ember_cuda_sample(EmberCudaState *s, const EmberSampleParams *p, float u, const int *hist, int hist_len,
+                       int *out_token);
+
 /* the state's pinned host logits buffer (vocab floats), owned by the state */
 float       *ember_cuda_state_host_logits(EmberCudaState *s);
 
@@ -192,6 +212,16 @@ void ember_host_rope_table(float *out, int ctx, int head_dim, float theta);
  * step's logits afterwards. Returns s's logits. */
 float *ember_forward_greedy(EmberModel *m, EmberState *s, int tok, int pos, int n,
                             int *out_tokens);
+/* ember_sample(sampler, logits, vocab) for the logits of the state's last
+ * ember_forward / ember_prefill, drawn on the device (no logits copied to the
+ * host, no host sort). *rng_state is the sampler's xorshift64* state and
+ * advances exactly as in the reference (one draw when temperature > 0);
+ * history / hist_len are the sampler's history array and length (NULL / 0 when
+ * it keeps none). As the reference's ember_sample would, the caller then records
+ * the token with ember_sampler_accept. Returns the token; fatal errors follow the
+ * library's convention. */
+int ember_sample_device(EmberState *s, const EmberSampleParams *p, uint64_t *rng_state, const int *history,
+                        int hist_len);
 /* the device-side state behind a public state (for timing hooks) */
 EmberCudaState *ember_state_cuda(EmberState *s);
 

@@ -712,3 +712,74 @@ int orc_argmax(const float *v, int n) {
     for (int i = 1; i < n; i++) if (v[i] > v[best]) best = i;
     return best;
 }
+
+/* ---- the sampler (ref src/sample.c:76-175), over host logits, in place ----
+ * Penalties over hist[0..hist_len) in array order; temperature <= 0: the first
+ * index of the maximum; else logits / temperature, softmax (glibc expf, the
+ * sum in index order, divide), candidates sorted by descending probability with
+ * the C library's qsort and the reference's comparator, top_k, min_p, top_p,
+ * then r = rng_f32 * cutoff and the first candidate whose running sum exceeds r.
+ * *rng is the xorshift64* state (advanced once when temperature > 0). */
+typedef struct { float prob; int idx; } OrcCand;
+
+static int orc_cmp_desc(const void *a, const void *b) {
+    float pa = ((const OrcCand *)a)->prob, pb = ((const OrcCand *)b)->prob;
+    return (pa < pb) - (pa > pb);
+}
+
+int orc_sample(float *logits, int n, float temperature, float top_p, int top_k, float min_p,
+               float repeat_penalty, float presence_penalty, float frequency_penalty, uint64_t *rng,
+               const int *hist, int hist_len) {
+    int has_rep = repeat_penalty != 1.0f, has_freq = frequency_penalty != 0.0f, has_pres = presence_penalty != 0.0f;
+    if (hist && hist_len > 0 && (has_rep || has_freq || has_pres)) {
+        for (int i = 0; i < hist_len; i++) {
+            int t = hist[i];
+            if (t < 0 || t >= n) continue;
+            int first = 1;
+            for (int j = 0; j < i; j++) if (hist[j] == t) { first = 0; break; }
+            if (first) {
+                if (has_rep) logits[t] = logits[t] > 0.0f ? logits[t] / repeat_penalty : logits[t] * repeat_penalty;
+                if (has_pres) logits[t] -= presence_penalty;
+            }
+            if (has_freq) logits[t] -= frequency_penalty;
+        }
+    }
+    if (temperature <= 0.0f) return orc_argmax(logits, n);
+    for (int i = 0; i < n; i++) logits[i] /= temperature;
+    float max = logits[orc_argmax(logits, n)];
+    float sum = 0.0f;
+    for (int i = 0; i < n; i++) { logits[i] = expf(logits[i] - max); sum += logits[i]; }
+    for (int i = 0; i < n; i++) logits[i] /= sum;
+    OrcCand *cand = malloc(sizeof(OrcCand) * (size_t)n);
+    if (!cand) fatal("out of memory");
+    for (int i = 0; i < n; i++) { cand[i].prob = logits[i]; cand[i].idx = i; }
+    qsort(cand, (size_t)n, sizeof(OrcCand), orc_cmp_desc);
+    int m = n;
+    if (top_k > 0 && top_k < m) m = top_k;
+    if (min_p > 0.0f && min_p < 1.0f) {
+        float thresh = min_p * cand[0].prob;
+        int keep = 1;
+        while (keep < m && cand[keep].prob >= thresh) keep++;
+        m = keep;
+    }
+    float cutoff;
+    if (top_p > 0.0f && top_p < 1.0f) {
+        float cum = 0.0f;
+        int last = m - 1;
+        for (int i = 0; i < m; i++) { cum += cand[i].prob; if (cum >= top_p) { last = i; break; } }
+        m = last + 1;
+        cutoff = cum;
+    } else {
+        cutoff = 0.0f;
+        for (int i = 0; i < m; i++) cutoff += cand[i].prob;
+    }
+    uint64_t x = *rng;
+    x ^= x >> 12; x ^= x << 25; x ^= x >> 27;
+    *rng = x;
+    float u = (float)((uint32_t)((x * 0x2545F4914F6CDD1DULL) >> 32) >> 8) / 16777216.0f;
+    float r = u * cutoff, cum = 0.0f;
+    int chosen = cand[m - 1].idx;
+    for (int i = 0; i < m; i++) { cum += cand[i].prob; if (r < cum) { chosen = cand[i].idx; break; } }
+    free(cand);
+    return chosen;
+}

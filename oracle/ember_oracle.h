@@ -37,5 +37,9 @@ float    orc_f16_to_f32(uint16_t h);
 void orc_rmsnorm(float *out, const float *x, const float *w, int n, float eps);
 float orc_expf(float x);
 void orc_set_threads(int n);
+/* the reference's sampler over host logits (modified in place); *rng advances */
+int orc_sample(float *logits, int n, float temperature, float top_p, int top_k, float min_p,
+               float repeat_penalty, float presence_penalty, float frequency_penalty, uint64_t *rng,
+               const int *hist, int hist_len);
 
 #endif
