@@ -477,7 +477,7 @@ def run_ours(args, world, rank, local, dist):
     L = cfg["n_layers"]
     for kind in range(6):
         ms, by = ctypes.c_float(), ctypes.c_double()
-        assert lib.ember_cuda_time_kernel(cs, kind, 5, ctypes.byref(ms), ctypes.byref(by)) == 0, \
+        assert lib.ember_cuda_time_kernel(cs, kind, 20, ctypes.byref(ms), ctypes.byref(by)) == 0, \
             lib.ember_cuda_error()
         per_step = ms.value * (1 if kind == 5 else L)
         kinds.append((per_step, kind, ms.value, by.value))
@@ -485,10 +485,9 @@ def run_ours(args, world, rank, local, dist):
     _, dk, dms, dbytes = kinds[0]
     peak, peak_kind = measured_peaks()
     achieved = dbytes / (dms / 1e3) / 1e9
-    # kernels of one greedy token: the forward graph's launches + argmax/advance
-    lib.ember_cuda_state_launches_per_step.restype = ctypes.c_int
-    lib.ember_cuda_state_launches_per_step.argtypes = [ctypes.c_void_p]
-    launches = lib.ember_cuda_state_launches_per_step(cs) + 1
+    # kernels of one greedy token (the greedy graph's launches, counted when captured)
+    launches = lib.ember_cuda_state_launches_per_token(cs)
+    assert launches > 0
     e.close()
 
     total_tokens = world * args.steps * ntok

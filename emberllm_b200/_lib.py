@@ -67,7 +67,7 @@ CUDA_SYMBOLS = [
     "ember_cuda_model_upload", "ember_cuda_model_free", "ember_cuda_model_bytes",
     "ember_cuda_state_new", "ember_cuda_state_free", "ember_cuda_forward", "ember_cuda_prefill",
     "ember_cuda_greedy", "ember_cuda_state_host_logits", "ember_cuda_state_stream",
-    "ember_cuda_state_logits_dev", "ember_cuda_state_launches_per_step", "ember_cuda_state_persistent",
+    "ember_cuda_state_logits_dev", "ember_cuda_state_launches_per_step", "ember_cuda_state_launches_per_token", "ember_cuda_state_persistent",
     "ember_cuda_error",
     "ember_cuda_available", "ember_cuda_profile_step", "ember_cuda_mark", "ember_cuda_elapsed_ms",
     "ember_cuda_time_kernel", "ember_cuda_argmax_static", "ember_host_expf_params",
@@ -142,6 +142,8 @@ def load(path=None):
     lib.ember_cuda_state_logits_dev.argtypes = [_P]
     lib.ember_cuda_state_launches_per_step.restype = ctypes.c_int
     lib.ember_cuda_state_launches_per_step.argtypes = [_P]
+    lib.ember_cuda_state_launches_per_token.restype = ctypes.c_int
+    lib.ember_cuda_state_launches_per_token.argtypes = [_P]
     lib.ember_cuda_state_persistent.restype = ctypes.c_int
     lib.ember_cuda_state_persistent.argtypes = [_P, ctypes.POINTER(ctypes.c_char_p)]
     lib.ember_cuda_sample.restype = ctypes.c_int

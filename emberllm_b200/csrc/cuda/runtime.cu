@@ -30,6 +30,7 @@
 #include "ember_ops.h"
 #include "kernels.cuh"
 #include "attn_split.cuh"
+#include "head.cuh"
 #include "runtime_internal.cuh"
 
 using namespace emb;
@@ -99,7 +100,9 @@ static int init_kernel_attrs(int device) {
         allow_max_smem(attn_softmax_pv_kernel<float, true>, optin) ||
         allow_max_smem(attn_softmax_pv_kernel<__half, true>, optin) ||
         allow_max_smem(attn_softmax_pv_kernel<float, false>, optin) ||
-        allow_max_smem(attn_softmax_pv_kernel<__half, false>, optin))
+        allow_max_smem(attn_softmax_pv_kernel<__half, false>, optin) ||
+        allow_max_smem(lm_head_kernel<false, false>, optin) || allow_max_smem(lm_head_kernel<true, false>, optin) ||
+        allow_max_smem(lm_head_kernel<false, true>, optin) || allow_max_smem(lm_head_kernel<true, true>, optin))
         return 1;
     if (device < 32) done_mask |= 1u << device;
     return 0;
@@ -356,6 +359,7 @@ extern "C" float *ember_cuda_state_host_logits(EmberCudaState *s) { return s->h_
 extern "C" void *ember_cuda_state_stream(EmberCudaState *s) { return (void *)s->stream; }
 extern "C" const float *ember_cuda_state_logits_dev(EmberCudaState *s) { return s->logits; }
 extern "C" int ember_cuda_state_launches_per_step(const EmberCudaState *s) { return s->launches_per_step; }
+extern "C" int ember_cuda_state_launches_per_token(const EmberCudaState *s) { return s->launches_greedy; }
 
 // ------------------------------------------------------------------ launches --
 
@@ -606,8 +610,69 @@ static int launch_layer(EmberCudaState *s, int kind, int l, int *count) {
     return set_err("unknown kernel kind %d", kind);
 }
 
-static int launch_head(EmberCudaState *s, int *count) {
+// The streaming lm_head kernel (head.cuh) for a Q8_0 / Q4_0 head of at most 32
+// blocks per row; its ring takes as many stages as shared memory holds (at
+// least two). Returns the depth, or 0 when the head keeps the tiled GEMV.
+template <bool ARGMAX, bool Q4>
+static int head_stages(int device, int stage_bytes, int cols) {
+    static int optin[32] = {0};
+    if (device < 0 || device >= 32) return 0;
+    if (!optin[device] &&
+        cudaDeviceGetAttribute(&optin[device], cudaDevAttrMaxSharedMemoryPerBlockOptin, device) != cudaSuccess)
+        return 0;
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, lm_head_kernel<ARGMAX, Q4>) != cudaSuccess) return 0;
+    // EMBER_HEAD_STAGES caps the depth (a tuning knob; default: all that fit)
+    const char *cap = getenv("EMBER_HEAD_STAGES");
+    int st = cap && atoi(cap) >= 2 && atoi(cap) < HEAD_MAX_STAGES ? atoi(cap) : HEAD_MAX_STAGES;
+    while (st >= 2 && head_smem_bytes(st, stage_bytes, cols) + fa.sharedSizeBytes > (size_t)optin[device]) st--;
+    return st >= 2 ? st : 0;
+}
+
+template <bool ARGMAX, bool Q4>
+static int launch_head_stream(EmberCudaState *s, bool *done) {
     EmberCudaModel *m = s->m;
+    const DevMat &w = m->lm_head;
+    *done = false;
+    const int cols = m->dim, nb = cols / 32;
+    if (cols % 32 || nb > 32 || nb < 1) return 0;
+    HeadArgs a;
+    memset(&a, 0, sizeof(a));
+    a.stage_bytes = head_stage_bytes(Q4 ? 1 : 0, cols);
+    a.stages = head_stages<ARGMAX, Q4>(m->device, a.stage_bytes, cols);
+    if (a.stages == 0) return 0;
+    a.q = w.q; a.s = w.s; a.rows = w.rows; a.cols = cols; a.groups = (w.rows + 31) / 32;
+    a.x = s->x; a.norm_w = m->final_norm; a.eps = m->eps;
+    a.logits = s->logits;
+    a.err = s->ctl + CTL_ERR;
+    a.part_v = s->am_v; a.part_i = s->am_i; a.ticket = s->am_ticket; a.ctl = s->ctl; a.out = s->out_tokens;
+    int grid = s->am_blocks < m->n_sm ? s->am_blocks : m->n_sm;
+    if (grid > a.groups) grid = a.groups;
+    CK(launch_pdl(lm_head_kernel<ARGMAX, Q4>, grid, HEAD_THREADS, head_smem_bytes(a.stages, a.stage_bytes, cols),
+                  s->stream, a));
+    *done = true;
+    return 0;
+}
+
+// final norm + lm_head; with `greedy`, also the argmax and the token / position
+// advance when the streaming kernel runs (*fused_tail = true), else the caller
+// adds argmax_advance
+static int launch_head(EmberCudaState *s, int *count, bool greedy = false, bool *fused_tail = nullptr) {
+    EmberCudaModel *m = s->m;
+    if (fused_tail) *fused_tail = false;
+    const int dt = m->lm_head.dtype;
+    if (dt == EMBER_DT_Q8_0 || dt == EMBER_DT_Q4_0) {
+        bool done = false;
+        const bool q4 = dt == EMBER_DT_Q4_0;
+        int rc = greedy ? (q4 ? launch_head_stream<true, true>(s, &done) : launch_head_stream<true, false>(s, &done))
+                        : (q4 ? launch_head_stream<false, true>(s, &done) : launch_head_stream<false, false>(s, &done));
+        if (rc) return rc;
+        if (done) {
+            (*count)++;
+            if (fused_tail) *fused_tail = greedy;
+            return 0;
+        }
+    }
     GemvArgs a = gemv_base(s);
     a.cols = m->dim;
     a.x = s->x; a.norm_w = m->final_norm; a.eps = m->eps;
@@ -626,8 +691,9 @@ static int record_step(EmberCudaState *s, bool with_layers, bool with_head, int 
             for (int kind = K_QKV; kind <= K_W2; kind++)
                 if (launch_layer(s, kind, l, count)) return 1;
     }
-    if (with_head && launch_head(s, count)) return 1;
-    if (tail == 1) {
+    bool fused = false;
+    if (with_head && launch_head(s, count, tail == 1, &fused)) return 1;
+    if (tail == 1 && !fused) {
         ArgmaxArgs aa;
         aa.logits = s->logits; aa.n = m->vocab; aa.part_v = s->am_v; aa.part_i = s->am_i;
         aa.ticket = s->am_ticket; aa.ctl = s->ctl; aa.out = s->out_tokens;
@@ -675,6 +741,7 @@ static int record_kind(EmberCudaState *s, int kind) {
         s->launches_per_step = count;
     } else if (kind == 1) {
         if (record_step(s, true, true, 1, nullptr, &count)) return 1;
+        s->launches_greedy = count;
     } else if (kind == 2) {
         if (record_step(s, true, false, 2, s->ids, &count)) return 1;
     } else {

@@ -100,6 +100,7 @@ struct EmberCudaState {
     // graphs
     cudaGraphExec_t g_fwd = nullptr, g_greedy = nullptr, g_prefill = nullptr, g_head = nullptr;
     int launches_per_step = 0;
+    int launches_greedy = 0;      // kernels of one device greedy token (0 until captured)
     emb::PfState *pf = nullptr;
     emb::PState *ps = nullptr;             // set when the persistent token step serves this state
     emb::SampleBufs *sb = nullptr;         // device sampling scratch

@@ -187,6 +187,9 @@ float       *ember_cuda_state_host_logits(EmberCudaState *s);
 void        *ember_cuda_state_stream(EmberCudaState *s);      /* cudaStream_t */
 const float *ember_cuda_state_logits_dev(EmberCudaState *s);  /* device pointer */
 int          ember_cuda_state_launches_per_step(const EmberCudaState *s);
+/* kernels of one device greedy token (the step, the lm_head with its fused
+ * argmax or a separate argmax); 0 until the state has run a greedy step */
+int          ember_cuda_state_launches_per_token(const EmberCudaState *s);
 /* 1 when the state's decode steps run as the persistent kernel (one cooperative
  * launch per forward step or greedy run); 0 when they run as captured graphs of
  * per-stage kernels, with *why (if not NULL) naming the reason */

@@ -105,6 +105,24 @@ def test_tiny_device_greedy_matches_oracle(prod, orc, name, persist, monkeypatch
     assert got == want
 
 
+@pytest.mark.parametrize("name,fused", [("tiny-llama", 1), ("tiny-smol-q4", 1), ("tiny-f32", 0),
+                                        ("qwen3-0.6b", 1)])
+def test_greedy_token_runs_the_fused_head(prod, name, fused, monkeypatch):
+    """a quantized lm_head streams through the head kernel whose epilogue picks
+    the token (no separate argmax launch); an fp32 head keeps the tiled GEMV and
+    the argmax kernel"""
+    monkeypatch.setenv("EMBER_PERSIST", "0")
+    from emberllm_b200 import Ember
+    e = Ember(synth.ensure_model(name), ctx=32)
+    e.generate_ids([1, 2, 3], 3)
+    e.forward(4, 6)
+    cs = e.lib.ember_state_cuda(e.st)
+    per_step = e.lib.ember_cuda_state_launches_per_step(cs)
+    per_token = e.lib.ember_cuda_state_launches_per_token(cs)
+    e.close()
+    assert per_token == per_step + (1 - fused)
+
+
 def _random_matrix(rng, rows, cols, dtype, orc):
     w = (rng.standard_normal((rows, cols)).astype(np.float32) * 0.02)
     if dtype == 0:
