@@ -61,6 +61,11 @@ def parse():
                    help="BASELINE's many-sequence workload instead: 8 x N independent streams "
                         "(N = --streams) split over the GPUs, each a 256-token prompt then "
                         "--tokens greedy steps decoded together")
+    p.add_argument("--agg-streams", default="16,64",
+                   help="with the headline: also decode 8 x N independent streams split over "
+                        "the GPUs for each N listed (BASELINE configs[4]); '' or 0 skips")
+    p.add_argument("--agg-tokens", type=int, default=64,
+                   help="greedy tokens per stream per timed step of the streams aggregate")
     p.add_argument("--prefill-only", action="store_true",
                    help="time only the batched prefill (NVTX range 'prefill' with --nvtx)")
     p.add_argument("--nvtx", action="store_true",
@@ -327,21 +332,22 @@ def time_prefill(args, lib, path, vocab, dist, nvtx):
     return max_over_ranks(dist, ms.value / 1e3 / 3)
 
 
-def run_streams(args, world, rank, local, dist):
-    """8 x N independent streams; GPU g decodes streams
-    [g*8N/G, (g+1)*8N/G) as one batch: strong scaling, no collective."""
+def streams_measure(args, world, rank, local, dist, total, ntok, steps, warmup):
+    """`total` independent streams split over the GPUs:
+    GPU g decodes streams [g*total/G, (g+1)*total/G) as one batch (no
+    collective). Each stream: its own 256-token prompt, then `ntok` greedy
+    tokens per timed step. Device time (CUDA events on the batch's stream,
+    max over ranks) and wall time of the same synchronous calls, which include
+    the host copies of the step's tokens in and out (the e2e figure)."""
     import numpy as np
+    import torch
     from emberllm_b200 import Ember, EmberBatch, load, synth
 
-    if rank == 0:
-        synth.ensure_model(args.config)
-    barrier(dist)
     path = synth.ensure_model(args.config)
     lib = load()
-    total = 8 * args.streams
     lo, hi = stream_range(total, world, rank)
     S = hi - lo
-    ntok, plen = args.tokens, 256
+    plen = 256
     e = Ember(path)
     b = EmberBatch(e, S, ctx=plen + ntok + 8, max_steps=ntok)
     firsts = []
@@ -349,42 +355,79 @@ def run_streams(args, world, rank, local, dist):
         rng = np.random.default_rng(1000 + lo + i)     # stream lo+i's own prompt
         firsts.append(b.prefill(i, [int(t) for t in rng.integers(0, e.vocab, plen)]))
     pos = [plen] * S
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         b.greedy(firsts, pos, min(8, ntok))
+    # events on the batch's stream (one CUDA stream when the batch runs as GEMMs;
+    # concurrent single-stream states use several, and then only wall time counts)
+    gemm = S > 8 or os.environ.get("EMBER_BATCH") == "gemm"
+    ev = None
+    if gemm and torch.cuda.is_available():
+        st = torch.cuda.ExternalStream(lib.ember_cuda_batch_stream(lib.ember_batch_cuda(b.b)))
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True), st)
     clocks = ClockSampler(local)
     clocks.start()
     barrier(dist)
     nvtx = Nvtx(args.nvtx)
+    if ev:
+        ev[0].record(ev[2])
     t0 = time.perf_counter()
     nvtx.push("streams")
-    for _ in range(args.steps):
+    for _ in range(steps):
         b.greedy(firsts, pos, ntok)     # synchronous: tokens come back to the host
     nvtx.pop()
-    t = time.perf_counter() - t0
+    t_wall = time.perf_counter() - t0
+    t_dev = None
+    if ev:
+        ev[1].record(ev[2])
+        ev[1].synchronize()
+        t_dev = ev[0].elapsed_time(ev[1]) / 1e3
     clk = clocks.stop()
-    t_max = max_over_ranks(dist, t)
+    t_wall = max_over_ranks(dist, t_wall)
+    t_dev = max_over_ranks(dist, t_dev) if t_dev is not None else None
     b.close()
     e.close()
-    value = total * ntok * args.steps / t_max
+    return {"S": S, "t_wall": t_wall, "t_dev": t_dev, "clk": clk, "gemm": gemm,
+            "tokens": total * ntok * steps}
+
+
+def streams_summary(m, total, world, ntok, steps):
+    value = m["tokens"] / (m["t_dev"] if m["t_dev"] else m["t_wall"])
+    e2e = m["tokens"] / m["t_wall"]
+    return {"streams": total, "streams_per_gpu": m["S"], "n_gpus": world, "tokens_per_step": ntok,
+            "value": round(value, 1), "unit": "tok/s", "per_stream_tok_s": round(value / total, 2),
+            "timing": "CUDA events on the batch stream, max over ranks" if m["t_dev"] else "wall clock",
+            "path": "batched GEMMs" if m["gemm"] else "concurrent single-stream states",
+            "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": m["S"] * 8,
+                    "d2h_bytes_per_step": m["S"] * ntok * 4,
+                    "path": "ember_batch_greedy (host tokens in, host tokens out), wall clock"},
+            "ms_per_step": round((m["t_dev"] or m["t_wall"]) / steps * 1e3, 3)}
+
+
+def run_streams(args, world, rank, local, dist):
+    """8 x N independent streams, N = --streams: strong
+    scaling over the GPUs, no collective."""
+    from emberllm_b200 import synth
+    if rank == 0:
+        synth.ensure_model(args.config)
+    barrier(dist)
+    total, ntok = 8 * args.streams, args.tokens
+    m = streams_measure(args, world, rank, local, dist, total, ntok, args.steps, args.warmup)
+    sm = streams_summary(m, total, world, ntok, args.steps)
     return {
         "metric": "aggregate decode tok/s (Qwen3-0.6B Q8_0, 8xN independent streams)",
-        "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(t_max / args.steps * 1e3, 3),
+        "value": sm["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": sm["ms_per_step"],
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int8 dot / fp32 (Q8_0 weights, exact reference arithmetic)",
         "data": "synthetic: N(0,0.02) weights seed 0, per-stream uniform random prompts",
         "config": {"workload": "%d streams (8 x %d), 256-token prompts, %d greedy tokens each, decoded "
-                               "together per GPU (%s)" % (total, args.streams, ntok,
-                                                          "concurrent single-stream states" if S <= 8 and
-                                                          os.environ.get("EMBER_BATCH") != "gemm"
-                                                          else "batched tcgen05 GEMMs"),
-                   "model": args.config, "streams": total, "streams_per_gpu": S, "tokens_per_step": ntok,
+                               "together per GPU (%s)" % (total, args.streams, ntok, sm["path"]),
+                   "model": args.config, "streams": total, "streams_per_gpu": m["S"], "tokens_per_step": ntok,
                    "parallelism": "streams split over %d GPU(s), one replica each" % world},
-        "per_stream_tok_s": round(value / total, 2),
-        "e2e": {"value": round(value, 1), "unit": "tok/s", "h2d_bytes_per_step": S * 8,
-                "d2h_bytes_per_step": S * ntok * 4,
-                "path": "ember_batch_greedy (host tokens in, host tokens out), wall clock"},
-        "clocks": clk,
+        "per_stream_tok_s": sm["per_stream_tok_s"],
+        "timing": sm["timing"],
+        "e2e": sm["e2e"],
+        "clocks": m["clk"],
     }
 
 
@@ -529,6 +572,15 @@ def run_ours(args, world, rank, local, dist):
         "kernel_shares": {KIND_NAMES[k]: round(ps, 4) for ps, k, _, _ in kinds},
         "clocks": clk,
     }
+    # BASELINE configs[4] beside the headline: 8 x 16 and 8 x 64 streams split
+    # over the N GPUs (the multi-GPU target; the headline stays single-stream)
+    aggs = []
+    for n_per in [int(v) for v in args.agg_streams.split(",") if v.strip() and int(v) > 0]:
+        total = 8 * n_per
+        m = streams_measure(args, world, rank, local, dist, total, args.agg_tokens, 2, args.warmup)
+        aggs.append(streams_summary(m, total, world, args.agg_tokens, 2))
+    if aggs:
+        line["streams_aggregate"] = aggs
     if rank == 0 and world == 1 and args.cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(depth, ntok, args.config)
     return line

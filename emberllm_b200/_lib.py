@@ -75,7 +75,7 @@ CUDA_SYMBOLS = [
     "ember_host_rope_table", "ember_forward_greedy", "ember_state_cuda", "ember_cuda_sample",
     "ember_sample_device",
     "ember_cuda_batch_new", "ember_cuda_batch_free", "ember_cuda_batch_prefill", "ember_cuda_batch_greedy",
-    "ember_cuda_batch_stream", "ember_batch_new", "ember_batch_free", "ember_batch_prefill",
+    "ember_cuda_batch_stream", "ember_batch_new", "ember_batch_cuda", "ember_batch_free", "ember_batch_prefill",
     "ember_batch_greedy",
 ]
 
@@ -136,6 +136,8 @@ def load(path=None):
     lib.ember_batch_greedy.argtypes = [_P, _IP, _IP, ctypes.c_int, _IP, _FP]
     lib.ember_cuda_batch_stream.restype = _P
     lib.ember_cuda_batch_stream.argtypes = [_P]
+    lib.ember_batch_cuda.restype = _P
+    lib.ember_batch_cuda.argtypes = [_P]
     lib.ember_cuda_state_stream.restype = _P
     lib.ember_cuda_state_stream.argtypes = [_P]
     lib.ember_cuda_state_logits_dev.restype = _P

@@ -106,20 +106,32 @@ static int pf_init(int device) {
     if (device < 32 && ((done >> device) & 1u)) return 0;
     int optin = 0;
     CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
-    if (pf_allow_smem(pf_gemm_kernel<32, PF_EPI_STORE>, PfLayout<32>::SMEM) ||
+    if (pf_allow_smem(pf_gemm_kernel<PF_SW_BN, PF_EPI_STORE, true>, PfLayout<PF_SW_BN>::SMEM) ||
+        pf_allow_smem(pf_gemm_kernel<PF_SW_BN, PF_EPI_RESID, true>, PfLayout<PF_SW_BN>::SMEM) ||
+        pf_allow_smem(pf_gemm_kernel<32, PF_EPI_STORE>, PfLayout<32>::SMEM) ||
         pf_allow_smem(pf_gemm_kernel<32, PF_EPI_RESID>, PfLayout<32>::SMEM) ||
         pf_allow_smem(pf_gemm_kernel<64, PF_EPI_STORE>, PfLayout<64>::SMEM) ||
         pf_allow_smem(pf_gemm_kernel<64, PF_EPI_RESID>, PfLayout<64>::SMEM) ||
         pf_allow_smem(pf_gemm_kernel<128, PF_EPI_STORE>, PfLayout<128>::SMEM) ||
         pf_allow_smem(pf_gemm_kernel<128, PF_EPI_RESID>, PfLayout<128>::SMEM))
         return 1;
+    // one cap for every attention instantiation: the 16-row ones hold the most
+    // static shared memory
     cudaFuncAttributes fa;
-    CK(cudaFuncGetAttributes(&fa, pf_attn_kernel<float>));
+    CK(cudaFuncGetAttributes(&fa, pf_attn_kernel<float, 16>));
     int cap = optin - (int)fa.sharedSizeBytes;
-    CK(cudaFuncGetAttributes(&fa, pf_attn_kernel<__half>));
+    CK(cudaFuncGetAttributes(&fa, pf_attn_kernel<__half, 16>));
     if (optin - (int)fa.sharedSizeBytes < cap) cap = optin - (int)fa.sharedSizeBytes;
-    if (pf_allow_smem(pf_attn_kernel<float>, cap) || pf_allow_smem(pf_attn_kernel<__half>, cap)) return 1;
+    if (pf_allow_smem(pf_attn_kernel<float, 4>, cap) || pf_allow_smem(pf_attn_kernel<__half, 4>, cap) ||
+        pf_allow_smem(pf_attn_kernel<float, 8>, cap) || pf_allow_smem(pf_attn_kernel<__half, 8>, cap) ||
+        pf_allow_smem(pf_attn_kernel<float, 16>, cap) || pf_allow_smem(pf_attn_kernel<__half, 16>, cap))
+        return 1;
     g_att_smem_cap = cap;
+    // the batched decode attention (attn_decode_kernel, BATCH mode)
+    CK(cudaFuncGetAttributes(&fa, attn_decode_kernel<float, true>));
+    if (pf_allow_smem(attn_decode_kernel<float, true>, optin - (int)fa.sharedSizeBytes)) return 1;
+    CK(cudaFuncGetAttributes(&fa, attn_decode_kernel<__half, true>));
+    if (pf_allow_smem(attn_decode_kernel<__half, true>, optin - (int)fa.sharedSizeBytes)) return 1;
     if (device < 32) done |= 1u << device;
     return 0;
 }
@@ -129,8 +141,10 @@ static int pf_init(int device) {
 struct PfMat {
     int8_t *q = nullptr;
     float *s = nullptr;
+    float *s_t = nullptr;      // the scales transposed, [nbp][rows_pad] (swapped GEMM)
     int rows = 0, rows_pad = 0, k = 0, k_pad = 0, nb = 0, nbp = 0;
     CUtensorMap map;           // A operand: boxes of 128 rows x 128 bytes
+    CUtensorMap map_sw;        // B operand of the swapped GEMM: boxes of PF_SW_BN rows
 };
 
 struct PfLayerPack {
@@ -165,7 +179,9 @@ static int build_pack(PfModel *pm, PfMat *pk, const DevMat *const *parts, int np
     pk->nb = k / 32;
     pk->nbp = (int)round_up((size_t)pk->nb, 4);
     const size_t qbytes = (size_t)pk->rows_pad * pk->k_pad, sbytes = (size_t)pk->rows_pad * pk->nbp * 4;
-    if (pf_alloc(pm->allocs, (void **)&pk->q, qbytes) || pf_alloc(pm->allocs, (void **)&pk->s, sbytes)) return 1;
+    if (pf_alloc(pm->allocs, (void **)&pk->q, qbytes) || pf_alloc(pm->allocs, (void **)&pk->s, sbytes) ||
+        pf_alloc(pm->allocs, (void **)&pk->s_t, sbytes))
+        return 1;
     CK(cudaMemset(pk->q, 0, qbytes));
     CK(cudaMemset(pk->s, 0, sbytes));
     int r0 = 0;
@@ -180,7 +196,14 @@ static int build_pack(PfModel *pm, PfMat *pk, const DevMat *const *parts, int np
         CK(cudaGetLastError());
         r0 += parts[i]->rows;
     }
-    return map_i8(&pk->map, pk->q, (size_t)pk->k_pad, (size_t)pk->rows_pad, PF_BM);
+    {
+        const long long total = (long long)pk->rows_pad * pk->nbp;
+        const int grid = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+        pf_transpose_kernel<<<grid, 256>>>(pk->s, pk->s_t, pk->rows_pad, pk->nbp);
+        CK(cudaGetLastError());
+    }
+    return map_i8(&pk->map, pk->q, (size_t)pk->k_pad, (size_t)pk->rows_pad, PF_BM) ||
+           map_i8(&pk->map_sw, pk->q, (size_t)pk->k_pad, (size_t)pk->rows_pad, PF_SW_BN);
 }
 
 int pf_supported(const EmberCudaModel *m) {
@@ -319,6 +342,28 @@ static int choose_bn(int rows_pad, int n, int n_sm) {
     return best;
 }
 
+// swapped operands (few tokens): A = the activations' 128-row box, B = PF_SW_BN
+// weight rows; one CTA per (token tile, PF_SW_BN weight rows)
+template <int EPI>
+static int launch_gemm_sw(const PfMat &w, const CUtensorMap &ma, const PfGemmArgs &a, cudaStream_t st) {
+    dim3 grid((unsigned)(a.n_pad / PF_BM), (unsigned)(w.rows_pad / PF_SW_BN));
+    pf_gemm_kernel<PF_SW_BN, EPI, true><<<grid, PfLayout<PF_SW_BN>::THREADS, PfLayout<PF_SW_BN>::SMEM, st>>>(
+        ma, w.map_sw, a);
+    CK(cudaGetLastError());
+    return 0;
+}
+
+// Swapped operands when the token tiles leave most SMs idle: the usual tiling
+// runs rows_pad/128 x ceil(n/BN) CTAs; the swapped one rows_pad/PF_SW_BN x
+// n_pad/128. EMBER_PF_SWAP=0/1 forces either (comparisons).
+static bool use_swap(int rows_pad, int n, int n_pad, int n_sm) {
+    const char *f = getenv("EMBER_PF_SWAP");
+    if (f && *f) return atoi(f) != 0;
+    const long long plain = (long long)(rows_pad / PF_BM) * ((n + 31) / 32);
+    const long long sw = (long long)(rows_pad / PF_SW_BN) * (n_pad / PF_BM);
+    return plain < n_sm && sw > plain;
+}
+
 template <int BN, int EPI>
 static int launch_gemm_bn(const PfMat &w, const CUtensorMap &mb, const PfGemmArgs &a, cudaStream_t st) {
     dim3 grid((unsigned)(w.rows_pad / PF_BM), (unsigned)((a.n + BN - 1) / BN));
@@ -330,8 +375,13 @@ static int launch_gemm_bn(const PfMat &w, const CUtensorMap &mb, const PfGemmArg
 static int launch_gemm(const PfMat &w, const CUtensorMap (&maps)[PF_NBN], const float *xs, int n_pad, int n,
                        float *out, int ld, bool resid, int *err, int n_sm, cudaStream_t st) {
     PfGemmArgs a;
-    a.ws = w.s; a.xs = xs; a.out = out; a.err = err;
+    a.ws = w.s; a.ws_t = w.s_t; a.rows_pad = w.rows_pad; a.xs = xs; a.out = out; a.err = err;
     a.rows = w.rows; a.nb = w.nb; a.nbp = w.nbp; a.n = n; a.n_pad = n_pad; a.ld = ld;
+    if (use_swap(w.rows_pad, n, n_pad, n_sm)) {
+        // the activations' 128-row box map (PF_BNS[PF_NBN - 1] == PF_BM)
+        return resid ? launch_gemm_sw<PF_EPI_RESID>(w, maps[PF_NBN - 1], a, st)
+                     : launch_gemm_sw<PF_EPI_STORE>(w, maps[PF_NBN - 1], a, st);
+    }
     const int j = choose_bn(w.rows_pad, n, n_sm);
     switch (j * 2 + (resid ? 1 : 0)) {
     case 0: return launch_gemm_bn<32, PF_EPI_STORE>(w, maps[0], a, st);
@@ -377,6 +427,11 @@ struct PfSeq {
     int ctx, kstride, kv_fp16;
     const float2 *rope;
     int tq, rs, p_cap;               // attention tiling
+    // batched decode: attention as the single-token kernel, one CTA per (query
+    // head, stream), with this chunking and shared memory (scores in shared memory)
+    int dec_attn, dec_chunk;
+    size_t dec_smem;
+    int *ctl;                        // error word
 };
 
 // embedding + every layer for q.n token rows of ids_dev, on ps->X
@@ -421,8 +476,27 @@ static int pf_layers(EmberCudaModel *m, PfState *ps, const PfSeq &q, const int *
         aa.p_cap = q.p_cap; aa.pos = q.pos; aa.cache_stride = q.cache_stride; aa.ex = m->ex;
         const dim3 agrid((unsigned)m->n_kv, (unsigned)((nc + q.tq - 1) / q.tq));
         const size_t asmem = pf_attn_smem(q.p_cap, q.rs);
-        if (q.kv_fp16) pf_attn_kernel<__half><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
-        else pf_attn_kernel<float><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
+        if (q.dec_attn) {
+            AttnArgs da;
+            memset(&da, 0, sizeof(da));
+            da.q = ps->QR; da.kc = qa.kc; da.vc = qa.vc; da.ctl = q.ctl;
+            da.nh = m->n_heads; da.nkv = m->n_kv; da.hd = hd; da.ctx = q.ctx; da.kstride = q.kstride;
+            da.att_in_smem = 1; da.chunk = q.dec_chunk; da.ex = m->ex;
+            da.bpos = q.pos; da.cache_stride = q.cache_stride;
+            da.bxq = ps->XQ; da.bxs = ps->XS; da.k_pad = ps->k_pad[PF_K_QD]; da.n_pad = ps->n_pad;
+            const dim3 dgrid((unsigned)m->n_heads, (unsigned)nc);
+            if (q.kv_fp16) attn_decode_kernel<__half, true><<<dgrid, ATTN_THREADS, q.dec_smem, st>>>(da);
+            else attn_decode_kernel<float, true><<<dgrid, ATTN_THREADS, q.dec_smem, st>>>(da);
+        } else if (q.rs <= 4) {
+            if (q.kv_fp16) pf_attn_kernel<__half, 4><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
+            else pf_attn_kernel<float, 4><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
+        } else if (q.rs <= 8) {
+            if (q.kv_fp16) pf_attn_kernel<__half, 8><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
+            else pf_attn_kernel<float, 8><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
+        } else {
+            if (q.kv_fp16) pf_attn_kernel<__half, 16><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
+            else pf_attn_kernel<float, 16><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
+        }
         CK(cudaGetLastError());
         if (launch_gemm(P.wo, ps->mapB[PF_K_QD], ps->XS, ps->n_pad, nc, ps->X, m->dim, true, err, m->n_sm, st))
             return 1;
@@ -748,6 +822,23 @@ static int batch_record(EmberCudaBatch *b) {
     q.p_cap = (int)round_up((size_t)b->ctx, 4);
     q.tq = 1;
     q.rs = (m->n_heads / m->n_kv + 3) / 4 * 4;
+    // attention per (query head, stream) with the cache staged through shared
+    // memory (attn_decode_kernel); EMBER_BATCH_ATTN=tile keeps the token-tile
+    // kernel of the prefill (for comparisons)
+    const char *ba = getenv("EMBER_BATCH_ATTN");
+    q.dec_attn = w->att_in_smem && w->m->head_dim <= ATTN_THREADS && !(ba && strcmp(ba, "tile") == 0);
+    // chunks of 48 positions (fp32, head_dim 128: 48 KB of buffers), so several
+    // (head, stream) CTAs share an SM; EMBER_BATCH_ATTN_CHUNK overrides (tuning)
+    {
+        const size_t es = b->kv_fp16 ? 2 : 4, hd = (size_t)m->head_dim;
+        const char *ce = getenv("EMBER_BATCH_ATTN_CHUNK");
+        int ch = ce && atoi(ce) >= 8 ? atoi(ce) / 8 * 8 : (int)((48 * 1024) / (2 * hd * es)) / 8 * 8;
+        if (ch < 8) ch = 8;
+        if (ch > w->attn_chunk) ch = w->attn_chunk;
+        q.dec_chunk = ch;
+        q.dec_smem = 2 * (size_t)ch * hd * es + ((size_t)b->ctx * 4 + 15) / 16 * 16;
+    }
+    q.ctl = w->ctl;
     if (pf_layers(m, b->ps, q, b->tok, err, st)) return 1;
     // final norm + lm_head over the S rows, then each stream's argmax
     PfState *ps = b->ps;

@@ -22,6 +22,7 @@
 #include <cuda.h>
 
 #include "common.cuh"
+#include "attn_decode.cuh"
 
 namespace emb {
 
@@ -197,6 +198,7 @@ EMB_DEV unsigned pf_smid() {
 #endif
 
 constexpr int PF_BM = 128;      // weight rows per tile (the MMA's M)
+constexpr int PF_SW_BN = 32;    // swapped GEMM: weight rows per tile (the MMA's N)
 constexpr int PF_BK = 128;      // K bytes per pipeline stage: four quant blocks
 constexpr int PF_STAGES = 4;
 // |acc| <= 32*127*127 < 2^22: acc + 1.5*2^23 read as a float is exact, and
@@ -208,6 +210,8 @@ enum { PF_EPI_STORE = 0, PF_EPI_RESID = 1 };
 
 struct PfGemmArgs {
     const float *ws;   // weight block scales, fp32 [rows_pad][nbp]
+    const float *ws_t; // the same transposed, [nbp][rows_pad] (SWAP)
+    int rows_pad;
     const float *xs;   // activation block scales, fp32 [nb][n_pad]
     float *out;        // STORE: out[t*ld + r] = y; RESID: out[t*ld + r] += y
     int *err;
@@ -256,7 +260,14 @@ struct PfLayout {
 //                the terms of block 2p then 2p+1 to each column's chain.
 // Every wait is bounded; a wait that gives up records ERR_PF_WAIT and the CTA
 // drains its copies and MMAs, frees its TMEM and exits.
-template <int BN, int EPI>
+//
+// SWAP (few token rows): the operands trade places -- A is 128 token rows of
+// the activations, B is BN weight rows -- so a matrix of R rows spreads over
+// R / BN CTAs instead of R / 128. Accumulator lanes are then tokens and columns
+// weight rows: the producer stages the weight scales of the stage's blocks
+// (from the transposed copy), each lane reads its token's activation scales,
+// and every term is still ((float)acc * d_w) * d_x, added in block order.
+template <int BN, int EPI, bool SWAP = false>
 __global__ void __launch_bounds__(PfLayout<BN>::THREADS, PfLayout<BN>::MIN_CTAS)
     pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const PfGemmArgs a) {
@@ -314,8 +325,14 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS, PfLayout<BN>::MIN_CTAS)
                 tma_load_2d(sm + Lay::OFF_A + slot * Lay::A_BYTES, &tmA, st * PF_BK, m0, &full[slot]);
                 tma_load_2d(sm + Lay::OFF_B + slot * Lay::B_BYTES, &tmB, st * PF_BK, n0, &full[slot]);
                 float *xsd = reinterpret_cast<float *>(sm + Lay::OFF_XS + slot * Lay::XS_BYTES);
-                for (int j = 0; j < nblk; j++)
-                    bulk_g2s(xsd + j * BN, a.xs + (size_t)(4 * st + j) * a.n_pad + n0, (uint32_t)(BN * 4), &full[slot]);
+                for (int j = 0; j < nblk; j++) {
+                    if (SWAP)   // this CTA's BN weight rows' scales of block 4st+j
+                        bulk_g2s(xsd + j * BN, a.ws_t + (size_t)(4 * st + j) * a.rows_pad + n0, (uint32_t)(BN * 4),
+                                 &full[slot]);
+                    else
+                        bulk_g2s(xsd + j * BN, a.xs + (size_t)(4 * st + j) * a.n_pad + n0, (uint32_t)(BN * 4),
+                                 &full[slot]);
+                }
                 issued = st + 1;
             }
             // drain: every stage this thread issued has landed before the CTA exits
@@ -357,16 +374,30 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS, PfLayout<BN>::MIN_CTAS)
     } else {
         // ---------------- epilogue ----------------
         const int quarter = warp & 3, cg = warp >> 2;
+        // this lane's accumulator row: a weight row, or (SWAP) a token
         const int row = m0 + 32 * quarter + lane;
-        const bool row_ok = row < a.rows;
-        const float *wsr = a.ws + (size_t)row * a.nbp;   // rows are padded: always in bounds
+        const bool row_ok = SWAP ? row < a.n : row < a.rows;
+        const float *wsr = a.ws + (size_t)(SWAP ? 0 : row) * a.nbp;   // rows are padded: always in bounds
+        const float *xsl = a.xs + row;                                // SWAP: [block][n_pad], row < n_pad
         float2 s2[16];
 #pragma unroll
         for (int j = 0; j < 16; j++) s2[j] = make_float2(0.0f, 0.0f);
         const float2 magic = make_float2(PF_MAGIC_F, PF_MAGIC_F);
-        // this row's weight scales, four blocks per load, fetched one stage ahead
-        float4 dw4 = *reinterpret_cast<const float4 *>(wsr);
-        float4 dw4n = a.nbp > 4 ? *reinterpret_cast<const float4 *>(wsr + 4) : dw4;
+        // this row's weight scales (SWAP: this token's activation scales), four
+        // blocks at a time, fetched one stage ahead
+        auto lane_scales = [&](int b) {
+            if (SWAP) {
+                float4 v;
+                v.x = xsl[(size_t)(b + 0) * a.n_pad];
+                v.y = b + 1 < a.nb ? xsl[(size_t)(b + 1) * a.n_pad] : 0.0f;
+                v.z = b + 2 < a.nb ? xsl[(size_t)(b + 2) * a.n_pad] : 0.0f;
+                v.w = b + 3 < a.nb ? xsl[(size_t)(b + 3) * a.n_pad] : 0.0f;
+                return v;
+            }
+            return *reinterpret_cast<const float4 *>(wsr + b);
+        };
+        float4 dw4 = lane_scales(0);
+        float4 dw4n = a.nbp > 4 ? lane_scales(4) : dw4;
         const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(cg * 32);
         for (int p = 0; p < n_pairs; p++) {
             const int st = p >> 1, slot = st % PF_STAGES, ps = p % NP;
@@ -378,7 +409,7 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS, PfLayout<BN>::MIN_CTAS)
             if ((p & 1) == 0) {
                 if (p > 0) {
                     dw4 = dw4n;
-                    if (b + 4 < a.nbp) dw4n = *reinterpret_cast<const float4 *>(wsr + b + 4);
+                    if (b + 4 < a.nbp) dw4n = lane_scales(b + 4);
                 }
                 // the stage's scale copies: observed by this warp too
                 if (lane == 0) ok = pf_wait(&full[slot], (uint32_t)((st / PF_STAGES) & 1), a.err, abort_v);
@@ -412,12 +443,21 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS, PfLayout<BN>::MIN_CTAS)
                         const uint32_t *rr = r + 16 * blk + 4 * q4;
                         float2 f0 = make_float2(__int_as_float((int)rr[0] + PF_MAGIC_I), __int_as_float((int)rr[1] + PF_MAGIC_I));
                         float2 f1 = make_float2(__int_as_float((int)rr[2] + PF_MAGIC_I), __int_as_float((int)rr[3] + PF_MAGIC_I));
-                        f0 = mul_f32x2(sub_f32x2(f0, magic), dw2);
-                        f1 = mul_f32x2(sub_f32x2(f1, magic), dw2);
-                        // the multiply whose result is added is scalar: ptxas may contract a
-                        // packed mul.f32x2 feeding an add into an fma, a scalar mul.rn never
-                        f0 = make_float2(fmul(f0.x, xv.x), fmul(f0.y, xv.y));
-                        f1 = make_float2(fmul(f1.x, xv.z), fmul(f1.y, xv.w));
+                        if (SWAP) {
+                            // columns are weight rows: d_w from the staged scales,
+                            // then this lane's token scale
+                            f0 = mul_f32x2(sub_f32x2(f0, magic), make_float2(xv.x, xv.y));
+                            f1 = mul_f32x2(sub_f32x2(f1, magic), make_float2(xv.z, xv.w));
+                            f0 = make_float2(fmul(f0.x, dw2.x), fmul(f0.y, dw2.x));
+                            f1 = make_float2(fmul(f1.x, dw2.x), fmul(f1.y, dw2.x));
+                        } else {
+                            f0 = mul_f32x2(sub_f32x2(f0, magic), dw2);
+                            f1 = mul_f32x2(sub_f32x2(f1, magic), dw2);
+                            // the multiply whose result is added is scalar: ptxas may contract a
+                            // packed mul.f32x2 feeding an add into an fma, a scalar mul.rn never
+                            f0 = make_float2(fmul(f0.x, xv.x), fmul(f0.y, xv.y));
+                            f1 = make_float2(fmul(f1.x, xv.z), fmul(f1.y, xv.w));
+                        }
                         s2[8 * h + 2 * q4] = add_f32x2(s2[8 * h + 2 * q4], f0);
                         s2[8 * h + 2 * q4 + 1] = add_f32x2(s2[8 * h + 2 * q4 + 1], f1);
                     }
@@ -432,10 +472,10 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS, PfLayout<BN>::MIN_CTAS)
         if (row_ok && !*abort_v) {
 #pragma unroll
             for (int j = 0; j < 32; j++) {
-                const int t = n0 + cg * 32 + j;
+                const int c = n0 + cg * 32 + j;   // the column: a token, or (SWAP) a weight row
                 const float v = (j & 1) ? s2[j >> 1].y : s2[j >> 1].x;
-                if (t < a.n) {
-                    float *o = a.out + (size_t)t * a.ld + row;
+                if (SWAP ? c < a.rows : c < a.n) {
+                    float *o = SWAP ? a.out + (size_t)row * a.ld + c : a.out + (size_t)c * a.ld + row;
                     *o = EPI == PF_EPI_RESID ? fadd(*o, v) : v;
                 }
             }
@@ -451,6 +491,16 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS, PfLayout<BN>::MIN_CTAS)
 }
 
 // --------------------------------------------------------------- packing -------
+
+// dst[b][r] = src[r][b] for a [rows][cols] fp32 matrix (the weight scales'
+// transposed copy for the swapped GEMM)
+__global__ void __launch_bounds__(256) pf_transpose_kernel(const float *src, float *dst, int rows, int cols) {
+    const long long total = (long long)rows * cols;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int b = (int)(i / rows), r = (int)(i - (long long)b * rows);
+        dst[i] = src[(size_t)r * cols + b];
+    }
+}
 
 // One row group of a prefill weight pack: int8 rows [rows_pad][k_pad] (Q4_0
 // nibbles expanded to q - 8, zero padding) and fp32 block scales [rows_pad][nbp].
@@ -687,14 +737,16 @@ __host__ __device__ inline size_t pf_attn_smem(int p_cap, int rs) { return (size
 // reads four rows per load. Loads of keys and values run eight ahead of the
 // chains. Products are rounded by scalar multiplies and added in pairs
 // (add.f32x2): the same two roundings per step as the reference.
-template <typename T>
+// RS: the register rows (4, 8 or 16, >= rs): a prefill tile takes 16 rows, a
+// batched decode row (one token of one stream) only its kv head's query heads.
+template <typename T, int RS>
 __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArgs a) {
+    static_assert(RS == 4 || RS == 8 || RS == 16, "pf_attn_kernel: RS is 4, 8 or 16");
     extern __shared__ __align__(16) float pf_att[];              // [p_cap][rs]
-    __shared__ __align__(16) float q_s[256 * PF_ATT_MAX_ROWS];   // [hd][16]
-    __shared__ float red[PF_ATT_MAX_ROWS][PF_ATT_THREADS / 32];
-    __shared__ float s_max[PF_ATT_MAX_ROWS], s_inv[PF_ATT_MAX_ROWS];
+    __shared__ __align__(16) float q_s[256 * RS];                // [hd][RS]
+    __shared__ float red[RS][PF_ATT_THREADS / 32];
+    __shared__ float s_max[RS], s_inv[RS];
     __shared__ double tab_s[64];
-    constexpr int RS = PF_ATT_MAX_ROWS;   // q_s stride and register rows
     const int rs = a.rs;                  // weight stride in shared memory (<= RS)
     const int kvh = blockIdx.x, b0 = blockIdx.y * a.tq, tid = threadIdx.x, hd = a.hd;
     const int kv_mul = a.nh / a.nkv;

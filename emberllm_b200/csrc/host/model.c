@@ -275,6 +275,8 @@ void ember_batch_free(EmberBatch *b) {
     free(b);
 }
 
+EmberCudaBatch *ember_batch_cuda(EmberBatch *b) { return b ? b->dev : NULL; }
+
 float *ember_batch_prefill(EmberBatch *b, int stream, const int *ids, int n) {
     if (stream < 0 || stream >= b->n_streams) ember_die("stream %d out of range [0,%d)", stream, b->n_streams);
     if (n <= 0 || n > b->ctx) ember_die("prompt of %d tokens does not fit the context of %d", n, b->ctx);

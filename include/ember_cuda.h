@@ -234,6 +234,8 @@ EmberCudaState *ember_state_cuda(EmberState *s);
 typedef struct EmberBatch EmberBatch;
 EmberBatch *ember_batch_new(EmberModel *m, int n_streams, int ctx_len, int kv_fp16, int max_steps);
 void        ember_batch_free(EmberBatch *b);
+/* the device-side batch behind a public batch (for timing hooks) */
+EmberCudaBatch *ember_batch_cuda(EmberBatch *b);
 /* prompt of stream `stream` at positions 0..n-1; returns its last token's logits
  * (vocab floats owned by the batch, valid until the next call) */
 float      *ember_batch_prefill(EmberBatch *b, int stream, const int *ids, int n);

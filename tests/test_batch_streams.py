@@ -53,17 +53,23 @@ def run_batch(path, prompts, n_steps, kv16, ctx):
     return firsts, toks, logits
 
 
-@pytest.mark.parametrize("mode", ["replicas", "gemm"])
+@pytest.mark.parametrize("mode", ["replicas", "gemm", "gemm-tile"])
 @pytest.mark.parametrize("kv16", [0, 1])
 @pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen3", "tiny-qwen2", "tiny-smol-q4", "tiny-mqa"])
 def test_tiny_streams_match_single_sequence_runs(orc, name, kv16, mode, monkeypatch):
     """five streams with prompts of 1..30 tokens, 12 steps together; up to 8
     streams run as concurrent single-stream states unless EMBER_BATCH=gemm
-    forces the batched GEMM path"""
-    if mode == "gemm":
+    forces the batched GEMM path, whose attention runs per (head, stream)
+    (attn_decode_kernel) or, with EMBER_BATCH_ATTN=tile, as the prefill's
+    token-tile kernel"""
+    if mode.startswith("gemm"):
         monkeypatch.setenv("EMBER_BATCH", "gemm")
     else:
         monkeypatch.delenv("EMBER_BATCH", raising=False)
+    if mode == "gemm-tile":
+        monkeypatch.setenv("EMBER_BATCH_ATTN", "tile")
+    else:
+        monkeypatch.delenv("EMBER_BATCH_ATTN", raising=False)
     path = synth.ensure_model(name)
     vocab = H.header_of(path)["vocab_size"]
     rng = np.random.default_rng(31 + kv16)
@@ -96,3 +102,41 @@ def test_qwen3_eight_streams(orc, mode, monkeypatch):
         f, want, want_logits = oracle_stream(orc, path, p, n_steps, 0, ctx)
         assert firsts[i] == f and [toks[s][i] for s in range(n_steps)] == want, f"stream {i}"
         assert_same(logits[i], want_logits, f"qwen3 stream {i} last logits")
+
+
+def _single_stream_run(e, prompt, n_steps):
+    """the single-sequence device path (pinned to the oracle elsewhere): prefill,
+    first pick, then ember_forward_greedy; returns (first, tokens, last logits)"""
+    import ctypes
+    lg = np.ctypeslib.as_array(e.prefill(prompt), (e.vocab,)).copy()
+    first = H.first_argmax(lg)
+    out = (ctypes.c_int * n_steps)()
+    p = e.lib.ember_forward_greedy(e.m, e.st, first, len(prompt), n_steps, out)
+    return first, list(out), np.ctypeslib.as_array(p, (e.vocab,)).copy()
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("kv16", [0, 1])
+@pytest.mark.parametrize("n", [16, 64])
+def test_qwen3_many_streams(orc, n, kv16, monkeypatch):
+    """configs[4] at the per-GPU sizes of 8 x 16 and 8 x 64 streams over 8 GPUs:
+    n Qwen3-0.6B streams (prompts of 8..47 tokens) decoded together for 8 steps
+    on the batched path; every stream equals its own single-sequence run (tokens
+    and last logits, bit for bit), two of them also the oracle's"""
+    monkeypatch.delenv("EMBER_BATCH", raising=False)
+    monkeypatch.delenv("EMBER_BATCH_ATTN", raising=False)
+    path = synth.ensure_model("qwen3-0.6b")
+    vocab = H.header_of(path)["vocab_size"]
+    rng = np.random.default_rng(100 + n)
+    prompts = [[int(t) for t in rng.integers(0, vocab, 8 + (7 * i) % 40)] for i in range(n)]
+    n_steps, ctx = 8, 64
+    firsts, toks, logits = run_batch(path, prompts, n_steps, kv16, ctx)
+    e = Ember(path, ctx=ctx, kv_fp16=bool(kv16))
+    for i, p in enumerate(prompts):
+        f, want, want_logits = _single_stream_run(e, p, n_steps)
+        assert firsts[i] == f and [toks[s][i] for s in range(n_steps)] == want, f"stream {i}"
+        assert_same(logits[i], want_logits, f"qwen3 stream {i} of {n} last logits")
+    e.close()
+    for i in (0, n - 1):
+        f, want, _ = oracle_stream(orc, path, prompts[i], n_steps, kv16, ctx)
+        assert firsts[i] == f and [toks[s][i] for s in range(n_steps)] == want, f"stream {i} vs oracle"
