@@ -148,6 +148,8 @@ EMB_DEV void cp_async16(void *smem_dst, const void *gmem_src) {
 }
 EMB_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 EMB_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// wait until at most one committed group (the newest) is still in flight
+EMB_DEV void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 EMB_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 EMB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -407,11 +409,14 @@ EMB_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // MBAR_TRIES slices (seconds in total) the wait gives up, records `code` in the
 // device error word and returns false, so a lost copy can never hang the GPU.
 constexpr uint32_t MBAR_TRIES = 1u << 22;
-EMB_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
-    for (uint32_t i = 0; i < MBAR_TRIES; i++)
+EMB_DEV bool mbar_wait_n(uint64_t *bar, uint32_t parity, int *err, int code, uint32_t tries) {
+    for (uint32_t i = 0; i < tries; i++)
         if (mbar_try_wait(bar, parity)) return true;
     if (err) atomicExch(err, code);
     return false;
+}
+EMB_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+    return mbar_wait_n(bar, parity, err, code, MBAR_TRIES);
 }
 
 // Bounded wait that backs off between polls (__nanosleep), for a thread whose

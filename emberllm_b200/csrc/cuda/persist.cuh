@@ -98,8 +98,6 @@ EMB_DEV void cp_async4(void *smem_dst, const void *gmem_src) {
                  "l"(gmem_src)
                  : "memory");
 }
-// wait for all of this thread's cp.async groups but the newest one
-EMB_DEV void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 struct PArgs {
     const PLayer *layers;

@@ -353,12 +353,14 @@ static int launch_gemm_sw(const PfMat &w, const CUtensorMap &ma, const PfGemmArg
     return 0;
 }
 
-// Swapped operands when the token tiles leave most SMs idle: the usual tiling
-// runs rows_pad/128 x ceil(n/BN) CTAs; the swapped one rows_pad/PF_SW_BN x
-// n_pad/128. EMBER_PF_SWAP=0/1 forces either (comparisons).
+// Swapped operands, opt-in (EMBER_PF_SWAP=1): for few tokens it spreads a
+// matrix over rows_pad/PF_SW_BN CTAs instead of rows_pad/128, but each CTA's
+// epilogue walks as many (row, token) chains as before, so it measured slower
+// (16 streams: 3.70k vs 3.95k tok/s; 32: 6.98k vs 7.26k); taken, when asked,
+// where the usual tiling leaves most SMs idle.
 static bool use_swap(int rows_pad, int n, int n_pad, int n_sm) {
     const char *f = getenv("EMBER_PF_SWAP");
-    if (f && *f) return atoi(f) != 0;
+    if (!(f && atoi(f) != 0)) return false;
     const long long plain = (long long)(rows_pad / PF_BM) * ((n + 31) / 32);
     const long long sw = (long long)(rows_pad / PF_SW_BN) * (n_pad / PF_BM);
     return plain < n_sm && sw > plain;
@@ -400,7 +402,7 @@ static int attn_tile(const EmberCudaModel *m, int p_cap, int *tq, int *rs) {
     const int kv_mul = m->n_heads / m->n_kv;
     for (int t = PF_ATT_MAX_ROWS / kv_mul; t > 0; t--) {
         const int r = (t * kv_mul + 3) / 4 * 4;
-        if (pf_attn_smem(p_cap, r) <= (size_t)g_att_smem_cap) {
+        if (pf_attn_smem(p_cap, r, m->head_dim, 4) <= (size_t)g_att_smem_cap) {   // fp32 cache: the larger
             *tq = t;
             *rs = r;
             return 1;
@@ -475,7 +477,7 @@ static int pf_layers(EmberCudaModel *m, PfState *ps, const PfSeq &q, const int *
         aa.ctx = q.ctx; aa.kstride = q.kstride; aa.start = q.start; aa.n = nc; aa.tq = q.tq; aa.rs = q.rs;
         aa.p_cap = q.p_cap; aa.pos = q.pos; aa.cache_stride = q.cache_stride; aa.ex = m->ex;
         const dim3 agrid((unsigned)m->n_kv, (unsigned)((nc + q.tq - 1) / q.tq));
-        const size_t asmem = pf_attn_smem(q.p_cap, q.rs);
+        const size_t asmem = pf_attn_smem(q.p_cap, q.rs, hd, (int)es);
         if (q.dec_attn) {
             AttnArgs da;
             memset(&da, 0, sizeof(da));

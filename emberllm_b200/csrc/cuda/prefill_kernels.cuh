@@ -719,36 +719,72 @@ struct PfAttnArgs {
     ExpfDev ex;
 };
 
-// shared memory of one attention CTA: the weights [p_cap][rs]
-__host__ __device__ inline size_t pf_attn_smem(int p_cap, int rs) { return (size_t)p_cap * rs * 4; }
+// positions per staged chunk of keys or values
+constexpr int PF_ATT_CH = 64;
+
+// shared memory of one attention CTA: the queries [hd][16] (RS <= 16 rows), the
+// weights [p_cap][rs], then two chunk buffers of PF_ATT_CH positions x hd cache
+// elements (keys or values)
+__host__ __device__ inline size_t pf_attn_w_bytes(int p_cap, int rs) {
+    return ((size_t)p_cap * rs * 4 + 15) / 16 * 16;
+}
+__host__ __device__ inline size_t pf_attn_smem(int p_cap, int rs, int hd, int es) {
+    return (size_t)hd * PF_ATT_MAX_ROWS * 4 + pf_attn_w_bytes(p_cap, rs) + 2 * (size_t)PF_ATT_CH * hd * es;
+}
+
+// keys of positions [c0, c0+n) -> buf[hd][PF_ATT_CH] (the cache keeps keys
+// transposed, [hd][kstride]); values -> buf[PF_ATT_CH][hd]. 16-byte cp.async by
+// every thread, committed as one group. Rows are padded to kstride (a multiple
+// of 8 positions) and c0 is a multiple of 8, so whole vectors stay in bounds.
+template <typename T>
+EMB_DEV void pf_stage_k(T *buf, const T *kt, int kstride, int c0, int n, int hd) {
+    constexpr int E = 16 / (int)sizeof(T);
+    const int nv = (n + E - 1) / E, total = hd * nv;
+    for (int idx = threadIdx.x; idx < total; idx += PF_ATT_THREADS) {
+        const int i = idx / nv, v = idx - i * nv;
+        cp_async16(buf + (size_t)i * PF_ATT_CH + v * E, kt + (size_t)i * kstride + c0 + v * E);
+    }
+    cp_async_commit();
+}
+template <typename T>
+EMB_DEV void pf_stage_v(T *buf, const T *vt, int c0, int n, int hd) {
+    constexpr int E = 16 / (int)sizeof(T);
+    const int total = n * hd / E;
+    for (int idx = threadIdx.x; idx < total; idx += PF_ATT_THREADS)
+        cp_async16(buf + (size_t)idx * E, vt + (size_t)c0 * hd + (size_t)idx * E);
+    cp_async_commit();
+}
 
 // One CTA per (kv head, tile of tq consecutive tokens); its query rows are the
 // tile's tokens x the kv head's query heads (row r = token r / kv_mul, head
 // kvh * kv_mul + r % kv_mul). Token j attends to positions 0..start+b0+j. For
 // every row, as in the single-token step (ref src/model.c:221-259):
-//   scores   sc_t = sum_i q_i*k_t,i in index order, * (1/sqrt(hd)) -- one thread
-//            per position, the 16 rows' chains side by side (each key element
-//            loaded once serves every row);
+//   scores   sc_t = sum_i q_i*k_t,i in index order, * (1/sqrt(hd)) -- per
+//            chunk of 64 cached positions staged in shared memory, one thread
+//            per (position, four rows): each key element loaded once serves
+//            four rows' chains, each query quad is a broadcast;
 //   softmax  max, e_t = expf(sc_t - max), den = sequential sum over t,
 //            w_t = e_t * (1/den);
 //   output   o_i = sum_t w_t*v_t,i in position order -- one thread per
-//            (dimension, row group), then quantized per (token, head).
-// Weights sit in shared memory as [position][rs rows], so the output loop
-// reads four rows per load. Loads of keys and values run eight ahead of the
-// chains. Products are rounded by scalar multiplies and added in pairs
+//            (dimension, row group) over staged value chunks, then quantized
+//            per (token, head).
+// Chunks are double-buffered: the copies of chunk c+1 run while chunk c is
+// used. Products are rounded by scalar multiplies and added in pairs
 // (add.f32x2): the same two roundings per step as the reference.
 // RS: the register rows (4, 8 or 16, >= rs): a prefill tile takes 16 rows, a
 // batched decode row (one token of one stream) only its kv head's query heads.
 template <typename T, int RS>
 __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArgs a) {
     static_assert(RS == 4 || RS == 8 || RS == 16, "pf_attn_kernel: RS is 4, 8 or 16");
-    extern __shared__ __align__(16) float pf_att[];              // [p_cap][rs]
-    __shared__ __align__(16) float q_s[256 * RS];                // [hd][RS]
+    extern __shared__ __align__(16) float pf_dyn[];              // q_s [hd][RS], weights, chunk buffers
+    float *q_s = pf_dyn;                                          // [hd][RS]
+    float *pf_att = pf_dyn + (size_t)a.hd * PF_ATT_MAX_ROWS;      // [p_cap][rs]
     __shared__ float red[RS][PF_ATT_THREADS / 32];
     __shared__ float s_max[RS], s_inv[RS];
     __shared__ double tab_s[64];
     const int rs = a.rs;                  // weight stride in shared memory (<= RS)
-    const int kvh = blockIdx.x, b0 = blockIdx.y * a.tq, tid = threadIdx.x, hd = a.hd;
+    // the heaviest tiles (the prompt's end, the longest causal rows) start first
+    const int kvh = blockIdx.x, b0 = (gridDim.y - 1 - blockIdx.y) * a.tq, tid = threadIdx.x, hd = a.hd;
     const int kv_mul = a.nh / a.nkv;
     const int ntok = min(a.tq, a.n - b0);
     const int rows = ntok * kv_mul;
@@ -760,43 +796,55 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
     const int p_last = pos0 + ntok - 1;              // the tile's last position
     const T *kt = reinterpret_cast<const T *>(a.kc) + coff + (size_t)kvh * hd * a.kstride;
     const T *vt = reinterpret_cast<const T *>(a.vc) + coff + (size_t)kvh * a.ctx * hd;
+    // the two chunk buffers: kvb0 + (c & 1) * cbuf
+    T *kvb0 = reinterpret_cast<T *>(reinterpret_cast<unsigned char *>(pf_att) + pf_attn_w_bytes(a.p_cap, rs));
+    const size_t cbuf = (size_t)PF_ATT_CH * hd;
+    const int npos = p_last + 1, nch = (npos + PF_ATT_CH - 1) / PF_ATT_CH;
+    pf_stage_k(kvb0, kt, a.kstride, 0, min(PF_ATT_CH, npos), hd);
     expf_table_load(tab_s, a.ex);
     for (int idx = tid; idx < RS * hd; idx += PF_ATT_THREADS) {
         const int r = idx / hd, i = idx - r * hd;
         const int j = r / kv_mul, hm = r - j * kv_mul;
         q_s[i * RS + r] = r < rows ? a.qr[(size_t)(b0 + j) * qd + (kvh * kv_mul + hm) * hd + i] : 0.0f;
     }
-    __syncthreads();
 
-    // ---- scores ----
+    // ---- scores: thread = (position in the chunk, row quad) ----
+    constexpr int QUADS = RS / 4, PP = PF_ATT_THREADS / QUADS;   // positions a pass covers
+    const int tl = tid % PP, rq = tid / PP;
     const float inv_sqrt = fdiv(1.0f, fsqrt((float)hd));
-    for (int t = tid; t <= p_last; t += PF_ATT_THREADS) {
-        float2 sc[RS / 2];
+    for (int c = 0; c < nch; c++) {
+        const int c0 = c * PF_ATT_CH, n = min(PF_ATT_CH, npos - c0);
+        if (c + 1 < nch) {
+            pf_stage_k(kvb0 + ((c + 1) & 1) * cbuf, kt, a.kstride, c0 + PF_ATT_CH,
+                       min(PF_ATT_CH, npos - c0 - PF_ATT_CH), hd);
+            cp_async_wait_1();
+        } else {
+            cp_async_wait_all();
+        }
+        __syncthreads();
+        const T *kb = kvb0 + (c & 1) * cbuf;
+        if (tl < n) {
+            float2 s0 = make_float2(0.0f, 0.0f), s1 = s0;
+            const float4 *qv = reinterpret_cast<const float4 *>(q_s) + rq;
+            for (int i = 0; i < hd; i += 8) {
+                float kk[8];
 #pragma unroll
-        for (int r = 0; r < RS / 2; r++) sc[r] = make_float2(0.0f, 0.0f);
-        for (int i = 0; i < hd; i += 8) {
-            float kk[8];
+                for (int j = 0; j < 8; j++) kk[j] = widen(kb[(size_t)(i + j) * PF_ATT_CH + tl]);
 #pragma unroll
-            for (int j = 0; j < 8; j++) kk[j] = widen(kt[(size_t)(i + j) * a.kstride + t]);
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const float4 *qv = reinterpret_cast<const float4 *>(q_s + (i + j) * RS);
-#pragma unroll
-                for (int r4 = 0; r4 < RS / 4; r4++) {
-                    const float4 q4 = qv[r4];
-                    sc[2 * r4] = add_f32x2(sc[2 * r4], make_float2(fmul(q4.x, kk[j]), fmul(q4.y, kk[j])));
-                    sc[2 * r4 + 1] = add_f32x2(sc[2 * r4 + 1], make_float2(fmul(q4.z, kk[j]), fmul(q4.w, kk[j])));
+                for (int j = 0; j < 8; j++) {
+                    const float4 q4 = qv[(i + j) * QUADS];
+                    s0 = add_f32x2(s0, make_float2(fmul(q4.x, kk[j]), fmul(q4.y, kk[j])));
+                    s1 = add_f32x2(s1, make_float2(fmul(q4.z, kk[j]), fmul(q4.w, kk[j])));
                 }
             }
+            if (4 * rq < rs)
+                *reinterpret_cast<float4 *>(pf_att + (size_t)(c0 + tl) * rs + 4 * rq) =
+                    make_float4(fmul(s0.x, inv_sqrt), fmul(s0.y, inv_sqrt), fmul(s1.x, inv_sqrt), fmul(s1.y, inv_sqrt));
         }
-        float4 *dst = reinterpret_cast<float4 *>(pf_att + (size_t)t * rs);
-#pragma unroll
-        for (int r4 = 0; r4 < RS / 4; r4++)
-            if (4 * r4 < rs)
-                dst[r4] = make_float4(fmul(sc[2 * r4].x, inv_sqrt), fmul(sc[2 * r4].y, inv_sqrt),
-                                  fmul(sc[2 * r4 + 1].x, inv_sqrt), fmul(sc[2 * r4 + 1].y, inv_sqrt));
+        __syncthreads();   // the buffer is free for chunk c + 2
     }
-    __syncthreads();
+    // the first value chunk streams in during the softmax
+    pf_stage_v(kvb0, vt, 0, min(PF_ATT_CH, npos), hd);
 
     // ---- softmax ----
     const int warp = tid >> 5, lane = tid & 31;
@@ -814,7 +862,7 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
         s_max[tid] = m;
     }
     __syncthreads();
-    for (int idx = tid; idx < (p_last + 1) * rs; idx += PF_ATT_THREADS) {
+    for (int idx = tid; idx < npos * rs; idx += PF_ATT_THREADS) {
         const int t = idx / rs, r = idx - t * rs;
         if (r < rows && t <= pos0 + r / kv_mul) pf_att[idx] = expf_exact(a.ex, tab_s, fsub(pf_att[idx], s_max[r]));
     }
@@ -835,55 +883,72 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
         s_inv[tid] = fdiv(1.0f, sum);
     }
     __syncthreads();
-    for (int idx = tid; idx < (p_last + 1) * rs; idx += PF_ATT_THREADS) {
+    for (int idx = tid; idx < npos * rs; idx += PF_ATT_THREADS) {
         const int t = idx / rs, r = idx - t * rs;
         if (r < rows && t <= pos0 + r / kv_mul) pf_att[idx] = fmul(pf_att[idx], s_inv[r]);
     }
-    __syncthreads();
 
-    // ---- outputs: thread = (dimension, row group) ----
+    // ---- outputs: thread = (dimension, row group), over staged value chunks ----
     const int groups = hd >= PF_ATT_THREADS ? 1 : PF_ATT_THREADS / hd;   // 1, 2 or 4
     const int rg = (rs + 4 * groups - 1) / (4 * groups) * 4;             // rows per group, a multiple of 4
     for (int i0 = 0; i0 < hd; i0 += PF_ATT_THREADS) {
         const int g = groups > 1 ? tid / hd : 0;
         const int i = groups > 1 ? tid - g * hd : i0 + tid;
         const int r0 = g * rg;
+        const bool live = i < hd && r0 < rows;
         float2 o[RS / 2];
 #pragma unroll
         for (int r = 0; r < RS / 2; r++) o[r] = make_float2(0.0f, 0.0f);
-        if (i < hd && r0 < rows) {
-            // positions every row takes
-            int t = 0;
-            for (; t + 8 <= p_first + 1; t += 8) {
-                float vv[8];
+        if (i0 > 0) {   // a second pass over the dimensions stages the values again
+            __syncthreads();
+            pf_stage_v(kvb0, vt, 0, min(PF_ATT_CH, npos), hd);
+        }
+        for (int c = 0; c < nch; c++) {
+            const int c0 = c * PF_ATT_CH, n = min(PF_ATT_CH, npos - c0);
+            if (c + 1 < nch) {
+                pf_stage_v(kvb0 + ((c + 1) & 1) * cbuf, vt, c0 + PF_ATT_CH, min(PF_ATT_CH, npos - c0 - PF_ATT_CH), hd);
+                cp_async_wait_1();
+            } else {
+                cp_async_wait_all();
+            }
+            __syncthreads();   // the chunk (and, for c = 0, the weights) are visible
+            const T *vb = kvb0 + (c & 1) * cbuf;
+            if (live) {
+                // positions every row takes, then each row up to its own position
+                const int t_all = min(n, p_first + 1 - c0);
+                int t = 0;
+                for (; t + 8 <= t_all; t += 8) {
+                    float vv[8];
 #pragma unroll
-                for (int j = 0; j < 8; j++) vv[j] = widen(vt[(size_t)(t + j) * hd + i]);
+                    for (int j = 0; j < 8; j++) vv[j] = widen(vb[(size_t)(t + j) * hd + i]);
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    const float4 *wv = reinterpret_cast<const float4 *>(pf_att + (size_t)(t + j) * rs + r0);
+                    for (int j = 0; j < 8; j++) {
+                        const float4 *wv = reinterpret_cast<const float4 *>(pf_att + (size_t)(c0 + t + j) * rs + r0);
 #pragma unroll
-                    for (int r4 = 0; r4 < RS / 4; r4++) {
-                        if (4 * r4 < rg && r0 + 4 * r4 < rs) {   // stay inside this position's row
-                            const float4 w4 = wv[r4];
-                            o[2 * r4] = add_f32x2(o[2 * r4], make_float2(fmul(w4.x, vv[j]), fmul(w4.y, vv[j])));
-                            o[2 * r4 + 1] = add_f32x2(o[2 * r4 + 1], make_float2(fmul(w4.z, vv[j]), fmul(w4.w, vv[j])));
+                        for (int r4 = 0; r4 < RS / 4; r4++) {
+                            if (4 * r4 < rg && r0 + 4 * r4 < rs) {   // stay inside this position's row
+                                const float4 w4 = wv[r4];
+                                o[2 * r4] = add_f32x2(o[2 * r4], make_float2(fmul(w4.x, vv[j]), fmul(w4.y, vv[j])));
+                                o[2 * r4 + 1] = add_f32x2(o[2 * r4 + 1], make_float2(fmul(w4.z, vv[j]), fmul(w4.w, vv[j])));
+                            }
+                        }
+                    }
+                }
+                for (; t < n; t++) {
+                    const int tp = c0 + t;
+                    const float v = widen(vb[(size_t)t * hd + i]);
+#pragma unroll
+                    for (int r = 0; r < RS; r++) {
+                        const int rr = r0 + r;
+                        if (r < rg && rr < rows && tp <= pos0 + rr / kv_mul) {
+                            const float w = pf_att[(size_t)tp * rs + rr];
+                            if (r & 1) o[r >> 1].y = fadd(o[r >> 1].y, fmul(w, v));
+                            else o[r >> 1].x = fadd(o[r >> 1].x, fmul(w, v));
                         }
                     }
                 }
             }
-            // the rest: each row up to its own position
-            for (; t <= p_last; t++) {
-                const float v = widen(vt[(size_t)t * hd + i]);
-#pragma unroll
-                for (int r = 0; r < RS; r++) {
-                    const int rr = r0 + r;
-                    if (r < rg && rr < rows && t <= pos0 + rr / kv_mul) {
-                        const float w = pf_att[(size_t)t * rs + rr];
-                        if (r & 1) o[r >> 1].y = fadd(o[r >> 1].y, fmul(w, v));
-                        else o[r >> 1].x = fadd(o[r >> 1].x, fmul(w, v));
-                    }
-                }
-            }
+            __syncthreads();   // the buffer is free for chunk c + 2
         }
         // quantize per (token, head): a warp holds 32 consecutive dimensions of
         // its group's rows

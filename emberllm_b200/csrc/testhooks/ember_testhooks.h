@@ -25,6 +25,14 @@ int ember_cuda_psum_batch(const float *host_terms, int n, int count, float *host
  * inputs for a kernel that reads state buffers. */
 int ember_testhook_copy_to_device(void *dev_dst, const void *host_src, unsigned long long bytes);
 
+/* A wait that runs out, on the device: mode 0 the mbarrier wait of the kernels'
+ * copies (mbar_wait_n) on a barrier nothing completes, mode 1 the persistent
+ * step's tagged hand-off wait (tw_wait1) on a word nothing writes; `tries`
+ * bounds it (try_wait slices / polls). *ok_out = 1 if the wait reported
+ * success, *err_out = the error word afterwards, *ms_out the kernel's time.
+ * Returns 0 when the launch itself completed. */
+int ember_testhook_wait_timeout(int mode, unsigned tries, int *ok_out, int *err_out, float *ms_out);
+
 #ifdef __cplusplus
 }
 #endif

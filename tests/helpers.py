@@ -202,6 +202,8 @@ def testhooks():
     lib.ember_cuda_split_sum_batch.argtypes = [_P, ctypes.c_int, ctypes.c_int, _P, _P]
     lib.ember_cuda_psum_batch.restype = ctypes.c_int
     lib.ember_cuda_psum_batch.argtypes = [_P, ctypes.c_int, ctypes.c_int, _P]
+    lib.ember_testhook_wait_timeout.restype = ctypes.c_int
+    lib.ember_testhook_wait_timeout.argtypes = [ctypes.c_int, ctypes.c_uint, _P, _P, _P]
     lib.ember_testhook_copy_to_device.restype = ctypes.c_int
     lib.ember_testhook_copy_to_device.argtypes = [_P, _P, ctypes.c_ulonglong]
     return lib

@@ -53,7 +53,7 @@ def run_batch(path, prompts, n_steps, kv16, ctx):
     return firsts, toks, logits
 
 
-@pytest.mark.parametrize("mode", ["replicas", "gemm", "gemm-tile"])
+@pytest.mark.parametrize("mode", ["replicas", "gemm", "gemm-tile", "gemm-swap"])
 @pytest.mark.parametrize("kv16", [0, 1])
 @pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen3", "tiny-qwen2", "tiny-smol-q4", "tiny-mqa"])
 def test_tiny_streams_match_single_sequence_runs(orc, name, kv16, mode, monkeypatch):
@@ -61,7 +61,7 @@ def test_tiny_streams_match_single_sequence_runs(orc, name, kv16, mode, monkeypa
     streams run as concurrent single-stream states unless EMBER_BATCH=gemm
     forces the batched GEMM path, whose attention runs per (head, stream)
     (attn_decode_kernel) or, with EMBER_BATCH_ATTN=tile, as the prefill's
-    token-tile kernel"""
+    token-tile kernel, and whose GEMMs may swap operands (EMBER_PF_SWAP=1)"""
     if mode.startswith("gemm"):
         monkeypatch.setenv("EMBER_BATCH", "gemm")
     else:
@@ -70,6 +70,10 @@ def test_tiny_streams_match_single_sequence_runs(orc, name, kv16, mode, monkeypa
         monkeypatch.setenv("EMBER_BATCH_ATTN", "tile")
     else:
         monkeypatch.delenv("EMBER_BATCH_ATTN", raising=False)
+    if mode == "gemm-swap":   # the opt-in swapped-operand GEMM
+        monkeypatch.setenv("EMBER_PF_SWAP", "1")
+    else:
+        monkeypatch.delenv("EMBER_PF_SWAP", raising=False)
     path = synth.ensure_model(name)
     vocab = H.header_of(path)["vocab_size"]
     rng = np.random.default_rng(31 + kv16)

@@ -62,3 +62,30 @@ def test_out_of_range_token_or_position_dies_like_the_reference(tok, pos):
     if H.have_reference():
         rrc, rout, rerr = _run(H.REF_DET, model, 48, tok, pos)
         assert (rrc, rerr) == (rc, err), (rrc, rerr)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode,code", [(0, 1), (1, 11)])
+def test_device_wait_runs_out_reports_and_the_context_stays_usable(mode, code):
+    """mode 0: the copies' mbarrier wait on a barrier nothing completes; mode 1:
+    the persistent step's tagged hand-off wait on a word nothing writes. Each,
+    bounded to a few thousand tries, returns failure and records its code
+    (ERR_GEMV_WAIT = 1, ERR_P_HANDOFF = 11) in the error word; the GPU then
+    runs the next work normally (a greedy run equal to the oracle's)."""
+    import ctypes
+    import numpy as np
+    from emberllm_b200 import Ember
+    hooks = H.testhooks()
+    ok, err, ms = ctypes.c_int(-1), ctypes.c_int(-1), ctypes.c_float(-1)
+    assert hooks.ember_testhook_wait_timeout(mode, 4000, ctypes.byref(ok), ctypes.byref(err), ctypes.byref(ms)) == 0
+    assert ok.value == 0, "the wait reported success on a barrier nothing completes"
+    assert err.value == code
+    assert 0.0 <= ms.value < 5000.0
+    path = synth.ensure_model("tiny-llama")
+    prompt = [int(t) for t in np.random.default_rng(9).integers(0, 512, 10)]
+    o = H.Oracle().session(path)
+    want = H.greedy_run(o, prompt, 8)
+    o.close()
+    e = Ember(path)
+    assert e.generate_ids(prompt, 8) == want
+    e.close()
