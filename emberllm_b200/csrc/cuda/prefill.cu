@@ -115,19 +115,27 @@ static int pf_init(int device) {
         pf_allow_smem(pf_gemm_kernel<128, PF_EPI_STORE>, PfLayout<128>::SMEM) ||
         pf_allow_smem(pf_gemm_kernel<128, PF_EPI_RESID>, PfLayout<128>::SMEM))
         return 1;
-    // one cap for every attention instantiation: the 16-row ones hold the most
-    // static shared memory
-    cudaFuncAttributes fa;
-    CK(cudaFuncGetAttributes(&fa, pf_attn_kernel<float, 16>));
-    int cap = optin - (int)fa.sharedSizeBytes;
-    CK(cudaFuncGetAttributes(&fa, pf_attn_kernel<__half, 16>));
-    if (optin - (int)fa.sharedSizeBytes < cap) cap = optin - (int)fa.sharedSizeBytes;
-    if (pf_allow_smem(pf_attn_kernel<float, 4>, cap) || pf_allow_smem(pf_attn_kernel<__half, 4>, cap) ||
-        pf_allow_smem(pf_attn_kernel<float, 8>, cap) || pf_allow_smem(pf_attn_kernel<__half, 8>, cap) ||
-        pf_allow_smem(pf_attn_kernel<float, 16>, cap) || pf_allow_smem(pf_attn_kernel<__half, 16>, cap))
-        return 1;
+    // one cap for every attention instantiation (the largest static shared memory)
+    int cap = optin;
+    auto cap_of = [&](const void *k) {
+        cudaFuncAttributes f;
+        if (cudaFuncGetAttributes(&f, k) == cudaSuccess && optin - (int)f.sharedSizeBytes < cap)
+            cap = optin - (int)f.sharedSizeBytes;
+    };
+#define EMB_PF_ATT_EACH(X)                                                                                   \
+    X(float, 4, 4) X(float, 8, 4) X(float, 8, 8) X(float, 16, 4) X(float, 16, 8) X(float, 16, 16)            \
+    X(__half, 4, 4) X(__half, 8, 4) X(__half, 8, 8) X(__half, 16, 4) X(__half, 16, 8) X(__half, 16, 16)      \
+    X(float, 4, 8) X(float, 4, 16) X(float, 8, 16) X(__half, 4, 8) X(__half, 4, 16) X(__half, 8, 16)
+#define EMB_CAP(T, RS, RG) cap_of((const void *)pf_attn_kernel<T, RS, RG>);
+    EMB_PF_ATT_EACH(EMB_CAP)
+#undef EMB_CAP
+#define EMB_ALLOW(T, RS, RG) if (pf_allow_smem(pf_attn_kernel<T, RS, RG>, cap)) return 1;
+    EMB_PF_ATT_EACH(EMB_ALLOW)
+#undef EMB_ALLOW
+#undef EMB_PF_ATT_EACH
     g_att_smem_cap = cap;
     // the batched decode attention (attn_decode_kernel, BATCH mode)
+    cudaFuncAttributes fa;
     CK(cudaFuncGetAttributes(&fa, attn_decode_kernel<float, true>));
     if (pf_allow_smem(attn_decode_kernel<float, true>, optin - (int)fa.sharedSizeBytes)) return 1;
     CK(cudaFuncGetAttributes(&fa, attn_decode_kernel<__half, true>));
@@ -436,6 +444,28 @@ struct PfSeq {
     int *ctl;                        // error word
 };
 
+// the attention instantiation for (cache type, register rows, output rows)
+template <typename T, int RS>
+static void launch_pf_attn_rs(int rg, dim3 grid, size_t smem, cudaStream_t st, const PfAttnArgs &aa) {
+    if (rg <= 4) pf_attn_kernel<T, RS, 4><<<grid, PF_ATT_THREADS, smem, st>>>(aa);
+    else if (rg <= 8) pf_attn_kernel<T, RS, 8><<<grid, PF_ATT_THREADS, smem, st>>>(aa);
+    else pf_attn_kernel<T, RS, 16><<<grid, PF_ATT_THREADS, smem, st>>>(aa);
+}
+static int launch_pf_attn(bool fp16, int rs, int rg, dim3 grid, size_t smem, cudaStream_t st, const PfAttnArgs &aa) {
+    if (rs <= 4) {
+        if (fp16) launch_pf_attn_rs<__half, 4>(rg, grid, smem, st, aa);
+        else launch_pf_attn_rs<float, 4>(rg, grid, smem, st, aa);
+    } else if (rs <= 8) {
+        if (fp16) launch_pf_attn_rs<__half, 8>(rg, grid, smem, st, aa);
+        else launch_pf_attn_rs<float, 8>(rg, grid, smem, st, aa);
+    } else {
+        if (fp16) launch_pf_attn_rs<__half, 16>(rg, grid, smem, st, aa);
+        else launch_pf_attn_rs<float, 16>(rg, grid, smem, st, aa);
+    }
+    CK(cudaGetLastError());
+    return 0;
+}
+
 // embedding + every layer for q.n token rows of ids_dev, on ps->X
 static int pf_layers(EmberCudaModel *m, PfState *ps, const PfSeq &q, const int *ids_dev, int *err, cudaStream_t st) {
     const int nc = q.n, hd = m->head_dim;
@@ -489,15 +519,8 @@ static int pf_layers(EmberCudaModel *m, PfState *ps, const PfSeq &q, const int *
             const dim3 dgrid((unsigned)m->n_heads, (unsigned)nc);
             if (q.kv_fp16) attn_decode_kernel<__half, true><<<dgrid, ATTN_THREADS, q.dec_smem, st>>>(da);
             else attn_decode_kernel<float, true><<<dgrid, ATTN_THREADS, q.dec_smem, st>>>(da);
-        } else if (q.rs <= 4) {
-            if (q.kv_fp16) pf_attn_kernel<__half, 4><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
-            else pf_attn_kernel<float, 4><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
-        } else if (q.rs <= 8) {
-            if (q.kv_fp16) pf_attn_kernel<__half, 8><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
-            else pf_attn_kernel<float, 8><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
         } else {
-            if (q.kv_fp16) pf_attn_kernel<__half, 16><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
-            else pf_attn_kernel<float, 16><<<agrid, PF_ATT_THREADS, asmem, st>>>(aa);
+            if (launch_pf_attn(q.kv_fp16 != 0, q.rs, pf_attn_rows_per_group(q.rs, hd), agrid, asmem, st, aa)) return 1;
         }
         CK(cudaGetLastError());
         if (launch_gemm(P.wo, ps->mapB[PF_K_QD], ps->XS, ps->n_pad, nc, ps->X, m->dim, true, err, m->n_sm, st))

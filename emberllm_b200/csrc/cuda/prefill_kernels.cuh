@@ -773,9 +773,17 @@ EMB_DEV void pf_stage_v(T *buf, const T *vt, int c0, int n, int hd) {
 // (add.f32x2): the same two roundings per step as the reference.
 // RS: the register rows (4, 8 or 16, >= rs): a prefill tile takes 16 rows, a
 // batched decode row (one token of one stream) only its kv head's query heads.
-template <typename T, int RS>
+// RG: the rows of one output thread's chains (pf_attn_rows_per_group), fixed at
+// compile time so the unrolled output loop issues no dead rows.
+__host__ __device__ inline int pf_attn_groups(int hd) { return hd >= PF_ATT_THREADS ? 1 : PF_ATT_THREADS / hd; }
+__host__ inline int pf_attn_rows_per_group(int rs, int hd) {
+    const int g = pf_attn_groups(hd), need = (rs + g - 1) / g;
+    return need <= 4 ? 4 : (need <= 8 ? 8 : 16);
+}
+template <typename T, int RS, int RG>
 __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArgs a) {
     static_assert(RS == 4 || RS == 8 || RS == 16, "pf_attn_kernel: RS is 4, 8 or 16");
+    static_assert(RG == 4 || RG == 8 || RG == 16, "pf_attn_kernel: RG is 4, 8 or 16");
     extern __shared__ __align__(16) float pf_dyn[];              // q_s [hd][RS], weights, chunk buffers
     float *q_s = pf_dyn;                                          // [hd][RS]
     float *pf_att = pf_dyn + (size_t)a.hd * PF_ATT_MAX_ROWS;      // [p_cap][rs]
@@ -862,9 +870,15 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
         s_max[tid] = m;
     }
     __syncthreads();
-    for (int idx = tid; idx < npos * rs; idx += PF_ATT_THREADS) {
-        const int t = idx / rs, r = idx - t * rs;
-        if (r < rows && t <= pos0 + r / kv_mul) pf_att[idx] = expf_exact(a.ex, tab_s, fsub(pf_att[idx], s_max[r]));
+    // every row's last position (rows of token j sit at pos0 + j)
+    int rlast[RS];
+#pragma unroll
+    for (int r = 0; r < RS; r++) rlast[r] = r < rows ? pos0 + r / kv_mul : -1;
+    for (int t = tid; t < npos; t += PF_ATT_THREADS) {
+        float *w = pf_att + (size_t)t * rs;
+#pragma unroll
+        for (int r = 0; r < RS; r++)
+            if (t <= rlast[r]) w[r] = expf_exact(a.ex, tab_s, fsub(w[r], s_max[r]));
     }
     __syncthreads();
     // denominators: the sequential sum over t, one chain per row (rows in parallel)
@@ -883,22 +897,24 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
         s_inv[tid] = fdiv(1.0f, sum);
     }
     __syncthreads();
-    for (int idx = tid; idx < npos * rs; idx += PF_ATT_THREADS) {
-        const int t = idx / rs, r = idx - t * rs;
-        if (r < rows && t <= pos0 + r / kv_mul) pf_att[idx] = fmul(pf_att[idx], s_inv[r]);
+    for (int t = tid; t < npos; t += PF_ATT_THREADS) {
+        float *w = pf_att + (size_t)t * rs;
+#pragma unroll
+        for (int r = 0; r < RS; r++)
+            if (t <= rlast[r]) w[r] = fmul(w[r], s_inv[r]);
     }
 
     // ---- outputs: thread = (dimension, row group), over staged value chunks ----
-    const int groups = hd >= PF_ATT_THREADS ? 1 : PF_ATT_THREADS / hd;   // 1, 2 or 4
-    const int rg = (rs + 4 * groups - 1) / (4 * groups) * 4;             // rows per group, a multiple of 4
+    const int groups = pf_attn_groups(hd);   // 1, 2, 4 or 8
+    constexpr int rg = RG;                   // rows per group (groups * RG >= rs)
     for (int i0 = 0; i0 < hd; i0 += PF_ATT_THREADS) {
         const int g = groups > 1 ? tid / hd : 0;
         const int i = groups > 1 ? tid - g * hd : i0 + tid;
         const int r0 = g * rg;
         const bool live = i < hd && r0 < rows;
-        float2 o[RS / 2];
+        float2 o[RG / 2];
 #pragma unroll
-        for (int r = 0; r < RS / 2; r++) o[r] = make_float2(0.0f, 0.0f);
+        for (int r = 0; r < RG / 2; r++) o[r] = make_float2(0.0f, 0.0f);
         if (i0 > 0) {   // a second pass over the dimensions stages the values again
             __syncthreads();
             pf_stage_v(kvb0, vt, 0, min(PF_ATT_CH, npos), hd);
@@ -925,8 +941,8 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
                     for (int j = 0; j < 8; j++) {
                         const float4 *wv = reinterpret_cast<const float4 *>(pf_att + (size_t)(c0 + t + j) * rs + r0);
 #pragma unroll
-                        for (int r4 = 0; r4 < RS / 4; r4++) {
-                            if (4 * r4 < rg && r0 + 4 * r4 < rs) {   // stay inside this position's row
+                        for (int r4 = 0; r4 < RG / 4; r4++) {
+                            if (r0 + 4 * r4 < rs) {   // stay inside this position's row
                                 const float4 w4 = wv[r4];
                                 o[2 * r4] = add_f32x2(o[2 * r4], make_float2(fmul(w4.x, vv[j]), fmul(w4.y, vv[j])));
                                 o[2 * r4 + 1] = add_f32x2(o[2 * r4 + 1], make_float2(fmul(w4.z, vv[j]), fmul(w4.w, vv[j])));
@@ -938,9 +954,9 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
                     const int tp = c0 + t;
                     const float v = widen(vb[(size_t)t * hd + i]);
 #pragma unroll
-                    for (int r = 0; r < RS; r++) {
+                    for (int r = 0; r < RG; r++) {
                         const int rr = r0 + r;
-                        if (r < rg && rr < rows && tp <= pos0 + rr / kv_mul) {
+                        if (rr < rows && tp <= pos0 + rr / kv_mul) {
                             const float w = pf_att[(size_t)tp * rs + rr];
                             if (r & 1) o[r >> 1].y = fadd(o[r >> 1].y, fmul(w, v));
                             else o[r >> 1].x = fadd(o[r >> 1].x, fmul(w, v));
@@ -955,9 +971,9 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) pf_attn_kernel(const PfAttnArg
         const bool warp_live = (groups > 1 ? (warp * 32) / hd < groups : i0 + warp * 32 < hd);
         if (warp_live) {
 #pragma unroll
-            for (int r = 0; r < RS; r++) {
+            for (int r = 0; r < RG; r++) {
                 const int rr = r0 + r;
-                if (r < rg && rr < rows) {
+                if (rr < rows) {
                     const float orr = (r & 1) ? o[r >> 1].y : o[r >> 1].x;
                     float dq;
                     const int8_t q = quant_lane(orr, &dq);
