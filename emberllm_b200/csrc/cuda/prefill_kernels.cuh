@@ -225,7 +225,10 @@ struct PfGemmArgs {
 
 template <int BN>
 struct PfLayout {
-    static constexpr int EW = BN / 8;                 // epilogue warps: 4 lane quarters x BN/32 column groups
+    // columns per epilogue warp: 16 for BN = 32 (eight epilogue warps share the
+    // tile's chains), else 32
+    static constexpr int CW = BN == 32 ? 16 : 32;
+    static constexpr int EW = 4 * BN / CW;            // epilogue warps: 4 lane quarters x BN/CW column groups
     static constexpr int THREADS = (EW + 2) * 32;     // + TMA producer warp + MMA warp
     static constexpr int A_BYTES = PF_BM * PF_BK;
     static constexpr int B_BYTES = BN * PF_BK;
@@ -255,7 +258,7 @@ struct PfLayout {
 //                kind::i8 MMAs (K = 32 each) into the pair's two accumulators,
 //                one commit to acc_full[pair slot].
 //   warps < EW   epilogue: warp w owns TMEM lanes 32*(w%4).. (tile rows) and
-//                columns 32*(w/4).. (tokens); per pair it reads the two blocks'
+//                columns CW*(w/4).. (tokens); per pair it reads the two blocks'
 //                int32 sums 16 columns at a time, frees the pair slot, and adds
 //                the terms of block 2p then 2p+1 to each column's chain.
 // Every wait is bounded; a wait that gives up records ERR_PF_WAIT and the CTA
@@ -373,15 +376,16 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS, PfLayout<BN>::MIN_CTAS)
         }
     } else {
         // ---------------- epilogue ----------------
+        constexpr int CW = Lay::CW, NH = CW / 16;   // columns of this warp, in 16-column halves
         const int quarter = warp & 3, cg = warp >> 2;
         // this lane's accumulator row: a weight row, or (SWAP) a token
         const int row = m0 + 32 * quarter + lane;
         const bool row_ok = SWAP ? row < a.n : row < a.rows;
         const float *wsr = a.ws + (size_t)(SWAP ? 0 : row) * a.nbp;   // rows are padded: always in bounds
         const float *xsl = a.xs + row;                                // SWAP: [block][n_pad], row < n_pad
-        float2 s2[16];
+        float2 s2[CW / 2];
 #pragma unroll
-        for (int j = 0; j < 16; j++) s2[j] = make_float2(0.0f, 0.0f);
+        for (int j = 0; j < CW / 2; j++) s2[j] = make_float2(0.0f, 0.0f);
         const float2 magic = make_float2(PF_MAGIC_F, PF_MAGIC_F);
         // this row's weight scales (SWAP: this token's activation scales), four
         // blocks at a time, fetched one stage ahead
@@ -398,7 +402,7 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS, PfLayout<BN>::MIN_CTAS)
         };
         float4 dw4 = lane_scales(0);
         float4 dw4n = a.nbp > 4 ? lane_scales(4) : dw4;
-        const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(cg * 32);
+        const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(cg * CW);
         for (int p = 0; p < n_pairs; p++) {
             const int st = p >> 1, slot = st % PF_STAGES, ps = p % NP;
             const int b = 2 * p, two = b + 1 < nb;
@@ -420,13 +424,13 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS, PfLayout<BN>::MIN_CTAS)
             tc_fence_after();
             const float dwa = (p & 1) ? dw4.z : dw4.x, dwb = (p & 1) ? dw4.w : dw4.y;
             const float4 *xsa = reinterpret_cast<const float4 *>(sm + Lay::OFF_XS + slot * Lay::XS_BYTES) +
-                                ((b & 3) * BN + cg * 32) / 4;
+                                ((b & 3) * BN + cg * CW) / 4;
             const float4 *xsb = xsa + BN / 4;
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
+            for (int h = 0; h < NH; h++) {
                 uint32_t r[32];
                 tmem_ld16x2(tl + (uint32_t)(2 * ps * BN + 16 * h), tl + (uint32_t)((2 * ps + 1) * BN + 16 * h), r);
-                if (h == 1) {
+                if (h == NH - 1) {
                     // both halves read: the pair slot is free for the MMA warp
                     tc_fence_before();
                     __syncwarp();
@@ -471,8 +475,8 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS, PfLayout<BN>::MIN_CTAS)
         }
         if (row_ok && !*abort_v) {
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-                const int c = n0 + cg * 32 + j;   // the column: a token, or (SWAP) a weight row
+            for (int j = 0; j < CW; j++) {
+                const int c = n0 + cg * CW + j;   // the column: a token, or (SWAP) a weight row
                 const float v = (j & 1) ? s2[j >> 1].y : s2[j >> 1].x;
                 if (SWAP ? c < a.rows : c < a.n) {
                     float *o = SWAP ? a.out + (size_t)row * a.ld + c : a.out + (size_t)c * a.ld + row;
