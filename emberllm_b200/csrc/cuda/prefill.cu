@@ -32,9 +32,10 @@
 namespace emb {
 
 constexpr int PF_CHUNK = 512;              // tokens per batched pass
-// token-tile widths of the GEMM: BN = 32 and 64 run two CTAs per SM, BN = 128 one
-constexpr int PF_NBN = 3;
-constexpr int PF_BNS[PF_NBN] = { 32, 64, 128 };
+// token-tile widths of the GEMM: BN = 16 runs three CTAs per SM, 32 and 64 two,
+// 128 one (the last is the 128-row box the swapped GEMM reads its A operand with)
+constexpr int PF_NBN = 4;
+constexpr int PF_BNS[PF_NBN] = { 16, 32, 64, 128 };
 
 static size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
 
@@ -108,6 +109,8 @@ static int pf_init(int device) {
     CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
     if (pf_allow_smem(pf_gemm_kernel<PF_SW_BN, PF_EPI_STORE, true>, PfLayout<PF_SW_BN>::SMEM) ||
         pf_allow_smem(pf_gemm_kernel<PF_SW_BN, PF_EPI_RESID, true>, PfLayout<PF_SW_BN>::SMEM) ||
+        pf_allow_smem(pf_gemm_kernel<16, PF_EPI_STORE>, PfLayout<16>::SMEM) ||
+        pf_allow_smem(pf_gemm_kernel<16, PF_EPI_RESID>, PfLayout<16>::SMEM) ||
         pf_allow_smem(pf_gemm_kernel<32, PF_EPI_STORE>, PfLayout<32>::SMEM) ||
         pf_allow_smem(pf_gemm_kernel<32, PF_EPI_RESID>, PfLayout<32>::SMEM) ||
         pf_allow_smem(pf_gemm_kernel<64, PF_EPI_STORE>, PfLayout<64>::SMEM) ||
@@ -394,12 +397,14 @@ static int launch_gemm(const PfMat &w, const CUtensorMap (&maps)[PF_NBN], const 
     }
     const int j = choose_bn(w.rows_pad, n, n_sm);
     switch (j * 2 + (resid ? 1 : 0)) {
-    case 0: return launch_gemm_bn<32, PF_EPI_STORE>(w, maps[0], a, st);
-    case 1: return launch_gemm_bn<32, PF_EPI_RESID>(w, maps[0], a, st);
-    case 2: return launch_gemm_bn<64, PF_EPI_STORE>(w, maps[1], a, st);
-    case 3: return launch_gemm_bn<64, PF_EPI_RESID>(w, maps[1], a, st);
-    case 4: return launch_gemm_bn<128, PF_EPI_STORE>(w, maps[2], a, st);
-    default: return launch_gemm_bn<128, PF_EPI_RESID>(w, maps[2], a, st);
+    case 0: return launch_gemm_bn<16, PF_EPI_STORE>(w, maps[0], a, st);
+    case 1: return launch_gemm_bn<16, PF_EPI_RESID>(w, maps[0], a, st);
+    case 2: return launch_gemm_bn<32, PF_EPI_STORE>(w, maps[1], a, st);
+    case 3: return launch_gemm_bn<32, PF_EPI_RESID>(w, maps[1], a, st);
+    case 4: return launch_gemm_bn<64, PF_EPI_STORE>(w, maps[2], a, st);
+    case 5: return launch_gemm_bn<64, PF_EPI_RESID>(w, maps[2], a, st);
+    case 6: return launch_gemm_bn<128, PF_EPI_STORE>(w, maps[3], a, st);
+    default: return launch_gemm_bn<128, PF_EPI_RESID>(w, maps[3], a, st);
     }
 }
 
@@ -485,7 +490,7 @@ static int pf_layers(EmberCudaModel *m, PfState *ps, const PfSeq &q, const int *
         ta.xq = ps->XQ; ta.xs = ps->XS; ta.n_pad = ps->n_pad; ta.ex = m->ex; ta.eps = m->eps;
         // attention block
         ta.x = ps->X; ta.ld_x = m->dim; ta.norm_w = L.attn_norm; ta.cols = m->dim; ta.k_pad = ps->k_pad[PF_K_DIM];
-        pf_norm_quant_kernel<<<nc, 256, (size_t)m->dim * 4, st>>>(ta);
+        pf_norm_quant_kernel<<<nc, 256, (size_t)m->dim * 8, st>>>(ta);
         CK(cudaGetLastError());
         if (launch_gemm(P.qkv, ps->mapB[PF_K_DIM], ps->XS, ps->n_pad, nc, ps->QKV, ps->ld_qkv, false, err, m->n_sm, st))
             return 1;
@@ -527,7 +532,7 @@ static int pf_layers(EmberCudaModel *m, PfState *ps, const PfSeq &q, const int *
             return 1;
         // feed-forward block
         ta.x = ps->X; ta.ld_x = m->dim; ta.norm_w = L.ffn_norm; ta.cols = m->dim; ta.k_pad = ps->k_pad[PF_K_DIM];
-        pf_norm_quant_kernel<<<nc, 256, (size_t)m->dim * 4, st>>>(ta);
+        pf_norm_quant_kernel<<<nc, 256, (size_t)m->dim * 8, st>>>(ta);
         CK(cudaGetLastError());
         if (launch_gemm(P.w13, ps->mapB[PF_K_DIM], ps->XS, ps->n_pad, nc, ps->H, ps->ld_h, false, err, m->n_sm, st))
             return 1;
@@ -871,7 +876,7 @@ static int batch_record(EmberCudaBatch *b) {
     memset(&ta, 0, sizeof(ta));
     ta.xq = ps->XQ; ta.xs = ps->XS; ta.n_pad = ps->n_pad; ta.ex = m->ex; ta.eps = m->eps;
     ta.x = ps->X; ta.ld_x = m->dim; ta.norm_w = m->final_norm; ta.cols = m->dim; ta.k_pad = ps->k_pad[PF_K_DIM];
-    pf_norm_quant_kernel<<<b->S, 256, (size_t)m->dim * 4, st>>>(ta);
+    pf_norm_quant_kernel<<<b->S, 256, (size_t)m->dim * 8, st>>>(ta);
     CK(cudaGetLastError());
     if (launch_gemm(m->pf->head, ps->mapB[PF_K_DIM], ps->XS, ps->n_pad, b->S, b->logits, b->ld_log, false, err,
                     m->n_sm, st))

@@ -227,7 +227,7 @@ template <int BN>
 struct PfLayout {
     // columns per epilogue warp: 16 for BN = 32 (eight epilogue warps share the
     // tile's chains), else 32
-    static constexpr int CW = BN == 32 ? 16 : 32;
+    static constexpr int CW = BN <= 32 ? 16 : 32;
     static constexpr int EW = 4 * BN / CW;            // epilogue warps: 4 lane quarters x BN/CW column groups
     static constexpr int THREADS = (EW + 2) * 32;     // + TMA producer warp + MMA warp
     static constexpr int A_BYTES = PF_BM * PF_BK;
@@ -237,10 +237,10 @@ struct PfLayout {
     static constexpr int OFF_B = OFF_A + PF_STAGES * A_BYTES;
     static constexpr int OFF_XS = OFF_B + PF_STAGES * B_BYTES;
     static constexpr int OFF_BAR = OFF_XS + PF_STAGES * XS_BYTES;
-    // CTAs per SM: two for BN = 32 / 64 (83 / 101 KB of shared memory), one for
-    // BN = 128 (137 KB); the TMEM ring of block-pair accumulators fills the SM's
-    // 512 columns between them
-    static constexpr int MIN_CTAS = BN == 128 ? 1 : 2;
+    // CTAs per SM: three for BN = 16 (74 KB of shared memory), two for BN = 32 /
+    // 64 (83 / 101 KB), one for BN = 128 (137 KB); the TMEM rings of block-pair
+    // accumulators share the SM's 512 columns
+    static constexpr int MIN_CTAS = BN == 128 ? 1 : (BN == 16 ? 3 : 2);
     static constexpr int NPAIR = (512 / MIN_CTAS) / (2 * BN) > 4 ? 4 : (512 / MIN_CTAS) / (2 * BN);
     static constexpr int N_BARS = 2 * PF_STAGES + 2 * NPAIR + 1;
     static constexpr int OFF_TMEM = OFF_BAR + N_BARS * 8;
@@ -574,15 +574,19 @@ EMB_DEV void pf_quant_row(const float *v, const PfTokArgs &a, int t) {
 }
 
 // RMSNorm of token t's residual row (ref src/model.c:50-55), then quantize.
+// dynamic shared memory: the row, then its squares (2 * cols floats). The sum of
+// squares is the sequential loop's, evaluated by split_chain_sum (common.cuh).
 __global__ void __launch_bounds__(256) pf_norm_quant_kernel(const PfTokArgs a) {
     extern __shared__ __align__(16) float pf_row[];
-    __shared__ float s_scale;
+    float *sq = pf_row + a.cols;
     const int t = blockIdx.x;
-    for (int i = threadIdx.x; i < a.cols; i += blockDim.x) pf_row[i] = a.x[(size_t)t * a.ld_x + i];
+    for (int i = threadIdx.x; i < a.cols; i += blockDim.x) {
+        const float v = a.x[(size_t)t * a.ld_x + i];
+        pf_row[i] = v;
+        sq[i] = fmul(v, v);
+    }
     __syncthreads();
-    if (threadIdx.x == 0) s_scale = rms_scale(chain_sumsq(pf_row, a.cols), a.cols, a.eps);
-    __syncthreads();
-    const float sc = s_scale;
+    const float sc = rms_scale(split_chain_sum<256>(sq, a.cols), a.cols, a.eps);
     for (int i = threadIdx.x; i < a.cols; i += blockDim.x) pf_row[i] = fmul(fmul(pf_row[i], sc), a.norm_w[i]);
     __syncthreads();
     pf_quant_row(pf_row, a, t);
@@ -596,9 +600,20 @@ __global__ void __launch_bounds__(256) pf_swiglu_quant_kernel(const PfTokArgs a)
     expf_table_load(tab_s, a.ex);
     __syncthreads();
     const float *xr = a.x + (size_t)t * a.ld_x;
-    for (int i = threadIdx.x; i < a.cols; i += blockDim.x) {
-        const float g = xr[i], u = xr[a.hidden + i];
-        pf_row[i] = fmul(fdiv(g, fadd(1.0f, expf_exact(a.ex, tab_s, -g))), u);
+    // the loads of four elements go out before their arithmetic
+    for (int i0 = threadIdx.x; i0 < a.cols; i0 += 4 * blockDim.x) {
+        float g[4], u[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int i = i0 + k * blockDim.x;
+            g[k] = i < a.cols ? __ldg(xr + i) : 0.0f;
+            u[k] = i < a.cols ? __ldg(xr + a.hidden + i) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int i = i0 + k * blockDim.x;
+            if (i < a.cols) pf_row[i] = fmul(fdiv(g[k], fadd(1.0f, expf_exact(a.ex, tab_s, -g[k]))), u[k]);
+        }
     }
     __syncthreads();
     pf_quant_row(pf_row, a, t);
