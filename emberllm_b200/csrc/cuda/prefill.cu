@@ -502,9 +502,10 @@ static int pf_layers(EmberCudaModel *m, PfState *ps, const PfSeq &q, const int *
         qa.vc = (char *)q.vc + (size_t)l * q.v_layer * es;
         qa.nh = m->n_heads; qa.nkv = m->n_kv; qa.hd = hd; qa.ctx = q.ctx; qa.kstride = q.kstride;
         qa.neox = m->rope_neox; qa.start = q.start; qa.pos = q.pos; qa.cache_stride = q.cache_stride; qa.eps = m->eps;
-        const dim3 qgrid((unsigned)nc, (unsigned)(m->n_heads + m->n_kv));
-        if (q.kv_fp16) pf_qkv_post_kernel<__half><<<qgrid, 256, 0, st>>>(qa);
-        else pf_qkv_post_kernel<float><<<qgrid, 256, 0, st>>>(qa);
+        qa.n = nc;
+        const unsigned qgrid = (unsigned)((nc * (m->n_heads + m->n_kv) + PF_QKV_WARPS - 1) / PF_QKV_WARPS);
+        if (q.kv_fp16) pf_qkv_post_kernel<__half><<<qgrid, 32 * PF_QKV_WARPS, 0, st>>>(qa);
+        else pf_qkv_post_kernel<float><<<qgrid, 32 * PF_QKV_WARPS, 0, st>>>(qa);
         CK(cudaGetLastError());
         PfAttnArgs aa;
         aa.qr = ps->QR; aa.kc = qa.kc; aa.vc = qa.vc; aa.xq = ps->XQ; aa.k_pad = ps->k_pad[PF_K_QD];

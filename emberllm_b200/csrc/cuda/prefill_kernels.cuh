@@ -658,19 +658,26 @@ struct PfQkvArgs {
     float *qr;             // [n][qd] roped queries
     void *kc, *vc;         // this layer's cache: keys [n_kv][hd][kstride], values [n_kv][ctx][hd]
     int nh, nkv, hd, ctx, kstride, neox, start;
+    int n;                 // tokens
     const int *pos;        // batched decode: token t's position pos[t] (device) and
     size_t cache_stride;   //   its own cache at kc/vc + t * cache_stride elements
     float eps;
 };
 
-// One CTA per (token, head) for the nh query heads and nkv key heads; the key
-// CTAs also store the values. Bias (ref :319-321), QK-norm (:326-329), RoPE
+// One warp per (token, head) for the nh query heads and nkv key heads, eight
+// pairs per CTA; the key warps also store the values. Bias (ref :319-321),
+// QK-norm (:326-329, the sum of squares in index order on lane 0), RoPE
 // (:66-80), KV store (:39-48) -- the single-token step's arithmetic.
+constexpr int PF_QKV_WARPS = 8;
 template <typename T>
-__global__ void __launch_bounds__(256) pf_qkv_post_kernel(const PfQkvArgs a) {
-    __shared__ float vals[256];
-    __shared__ float s_scale;
-    const int t = blockIdx.x, hh = blockIdx.y, tid = threadIdx.x, hd = a.hd;
+__global__ void __launch_bounds__(32 * PF_QKV_WARPS) pf_qkv_post_kernel(const PfQkvArgs a) {
+    __shared__ float vals_s[PF_QKV_WARPS][256];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, hd = a.hd;
+    const int nhh = a.nh + a.nkv;
+    const int pair = blockIdx.x * PF_QKV_WARPS + warp;
+    if (pair >= a.n * nhh) return;   // whole warps only; no CTA barrier follows
+    const int t = pair / nhh, hh = pair - t * nhh;
+    float *vals = vals_s[warp];
     const int pos = a.pos ? a.pos[t] : a.start + t;
     const size_t coff = a.pos ? (size_t)t * a.cache_stride : 0;
     const int qd = a.nh * hd, kvd = a.nkv * hd;
@@ -680,39 +687,40 @@ __global__ void __launch_bounds__(256) pf_qkv_post_kernel(const PfQkvArgs a) {
     const float *bias = is_q ? a.bq : a.bk;
     const float *nw = is_q ? a.q_norm : a.k_norm;
     const float *row = a.qkv + (size_t)t * a.ld;
-    if (tid < hd) {
-        float v = row[off + tid];
-        if (bias) v = fadd(v, bias[head * hd + tid]);
-        vals[tid] = v;
+    for (int i = lane; i < hd; i += 32) {
+        float v = row[off + i];
+        if (bias) v = fadd(v, bias[head * hd + i]);
+        vals[i] = v;
     }
-    __syncthreads();
+    __syncwarp();
     if (nw) {
-        if (tid == 0) s_scale = rms_scale(chain_sumsq(vals, hd), hd, a.eps);
-        __syncthreads();
-        if (tid < hd) vals[tid] = fmul(fmul(vals[tid], s_scale), nw[tid]);
-        __syncthreads();
+        float sc = 0.0f;
+        if (lane == 0) sc = rms_scale(chain_sumsq(vals, hd), hd, a.eps);
+        sc = __shfl_sync(0xffffffffu, sc, 0);
+        for (int i = lane; i < hd; i += 32) vals[i] = fmul(fmul(vals[i], sc), nw[i]);
+        __syncwarp();
     }
-    if (tid < hd / 2) {
-        const int ia = a.neox ? tid : 2 * tid, ib = a.neox ? tid + hd / 2 : 2 * tid + 1;
-        const float2 cs = a.rope[(size_t)pos * (hd / 2) + tid];
+    for (int i = lane; i < hd / 2; i += 32) {
+        const int ia = a.neox ? i : 2 * i, ib = a.neox ? i + hd / 2 : 2 * i + 1;
+        const float2 cs = a.rope[(size_t)pos * (hd / 2) + i];
         const float v0 = vals[ia], v1 = vals[ib];
         vals[ia] = fsub(fmul(v0, cs.x), fmul(v1, cs.y));
         vals[ib] = fadd(fmul(v0, cs.y), fmul(v1, cs.x));
     }
-    __syncthreads();
-    if (tid < hd) {
+    __syncwarp();
+    for (int i = lane; i < hd; i += 32) {
         if (is_q) {
-            a.qr[(size_t)t * qd + head * hd + tid] = vals[tid];
+            a.qr[(size_t)t * qd + head * hd + i] = vals[i];
         } else {
             T *kt = reinterpret_cast<T *>(a.kc) + coff + (size_t)head * hd * a.kstride;
             T *vt = reinterpret_cast<T *>(a.vc) + coff + (size_t)head * a.ctx * hd;
             T kq, vq;
-            kv_round(vals[tid], &kq);
-            float v = row[qd + kvd + head * hd + tid];
-            if (a.bv) v = fadd(v, a.bv[head * hd + tid]);
+            kv_round(vals[i], &kq);
+            float v = row[qd + kvd + head * hd + i];
+            if (a.bv) v = fadd(v, a.bv[head * hd + i]);
             kv_round(v, &vq);
-            kt[(size_t)tid * a.kstride + pos] = kq;
-            vt[(size_t)pos * hd + tid] = vq;
+            kt[(size_t)i * a.kstride + pos] = kq;
+            vt[(size_t)pos * hd + i] = vq;
         }
     }
 }
