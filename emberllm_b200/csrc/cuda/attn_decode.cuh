@@ -184,6 +184,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
     EMB_PROBE(4, 5);
     // ---- scores: sc = sum_i q_i*k_i in index order, then * (1/sqrt(hd)) ----
     const float inv_sqrt = fdiv(1.0f, fsqrt((float)hd));
+    float lmax = -INFINITY;   // the largest of this thread's scores (the max is order-free)
     for (int c = 0; c < nchunks; c++) {
         const int c0 = c * CH, n = min(CH, ncache - c0);
         if (c > 0) {
@@ -201,7 +202,9 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
 #pragma unroll
                 for (int j = 0; j < 8; j++) sc = fadd(sc, fmul(qs[i + j], kk[j]));
             }
-            att[c0 + t] = fmul(sc, inv_sqrt);
+            const float s = fmul(sc, inv_sqrt);
+            att[c0 + t] = s;
+            lmax = fmaxf(lmax, s);
         }
     }
     // the score at t == pos (keys in registers' smem copy), on a thread that had
@@ -211,7 +214,12 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
         float sc = 0.0f;
         for (int i = 0; i < hd; i++) sc = fadd(sc, fmul(qs[i], ks[i]));
         att[pos] = fmul(sc, inv_sqrt);
+        lmax = fmaxf(lmax, att[pos]);
     }
+    // ---- softmax (ref src/model.c:57-64): the max is order-free, so each warp
+    // reduces its threads' maxima and one barrier publishes them (and the scores)
+    lmax = warp_max(lmax);
+    if (lane == 0) red[warp] = lmax;
     __syncthreads();
     EMB_PROBE(4, 6);
     // the keys are done: value chunk 1 may stream into buf0 during the softmax
@@ -222,24 +230,17 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
         bulk_g2s(buf0, vt + (size_t)CH * hd, (uint32_t)(n1 * hd * sizeof(T)), &bars[0]);
     }
 
-    // ---- softmax (ref src/model.c:57-64): the max is order-free ----
-    float tmax = -INFINITY;
-    for (int t = tid; t <= pos; t += ATTN_THREADS) tmax = fmaxf(tmax, att[t]);
-    tmax = warp_max(tmax);
-    if (lane == 0) red[warp] = tmax;
-    __syncthreads();
-    if (tid == 0) {
-        float m = red[0];
-        for (int w = 1; w < ATTN_THREADS / 32; w++) m = fmaxf(m, red[w]);
-        s_max = m;
-    }
-    __syncthreads();
-    const float mx = s_max;
+    float mx = red[0];
+#pragma unroll
+    for (int w = 1; w < ATTN_THREADS / 32; w++) mx = fmaxf(mx, red[w]);
+    EMB_PROBE(4, 10);
     for (int t = tid; t <= pos; t += ATTN_THREADS) att[t] = expf_exact(a.ex, tab_s, fsub(att[t], mx));
     __syncthreads();
+    EMB_PROBE(4, 11);
     // the denominator: the reference's sequential sum over t = 0..pos
-    if (tid == 0) s_inv = fdiv(1.0f, chain_sum(0.0f, att, pos + 1));
+    if (tid == 0) s_inv = fdiv(1.0f, chain_sum_pipe(0.0f, att, pos + 1));
     __syncthreads();
+    EMB_PROBE(4, 12);
     const float inv = s_inv;
     for (int t = tid; t <= pos; t += ATTN_THREADS) att[t] = fmul(att[t], inv);
     __syncthreads();
