@@ -293,4 +293,168 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
     EMB_PROBE(4, 9);
 }
 
+// ---- batched decode: one CTA per (kv head, stream) -----------------------------
+
+constexpr int AB_CH = 64;   // cached positions per staged chunk
+
+// keys of positions [c0, c0+n) -> buf[hd][AB_CH] (the cache keeps keys transposed,
+// [hd][kstride]); values -> buf[AB_CH][hd]. 16-byte cp.async by every thread, one
+// committed group. Rows are padded to kstride (a multiple of 8) and c0 is a
+// multiple of 8, so whole vectors stay in bounds.
+template <typename T>
+EMB_DEV void ab_stage_k(T *buf, const T *kt, int kstride, int c0, int n, int hd) {
+    constexpr int E = 16 / (int)sizeof(T);
+    const int nv = (n + E - 1) / E, total = hd * nv;
+    for (int idx = threadIdx.x; idx < total; idx += ATTN_THREADS) {
+        const int i = idx / nv, v = idx - i * nv;
+        cp_async16(buf + (size_t)i * AB_CH + v * E, kt + (size_t)i * kstride + c0 + v * E);
+    }
+    cp_async_commit();
+}
+template <typename T>
+EMB_DEV void ab_stage_v(T *buf, const T *vt, int c0, int n, int hd) {
+    constexpr int E = 16 / (int)sizeof(T);
+    const int total = n * hd / E;
+    for (int idx = threadIdx.x; idx < total; idx += ATTN_THREADS)
+        cp_async16(buf + (size_t)idx * E, vt + (size_t)c0 * hd + (size_t)idx * E);
+    cp_async_commit();
+}
+
+// dynamic shared memory: two chunk buffers, then the scores [KVM][att_stride]
+__host__ inline size_t ab_smem_bytes(int hd, int es, int kvm, int att_stride) {
+    return 2 * (size_t)AB_CH * hd * es + (size_t)kvm * att_stride * 4;
+}
+
+// One CTA per (kv head, stream) of a batched decode step: the KVM query heads of
+// the kv head share every staged chunk of the stream's cache (ref
+// src/model.c:221-259, the single-token step's chains in its order):
+//   scores   thread (position of the chunk, head): sum_i q_i*k_i in index order;
+//   softmax  per head: the max (order-free: each thread keeps its own, a warp
+//            reduction, one barrier), expf, the sequential denominator (one
+//            lane per head), w = e * (1/den);
+//   output   thread (head, dimension): sum_t w_t*v_t in position order, then Q8
+//            into the token-row GEMM layout.
+// The query is already normed and roped and this position's key and value are
+// in the cache (pf_qkv_post_kernel). Key chunks, then value chunks, are
+// double-buffered: chunk c+1's copies run while chunk c is used. Needs
+// KVM * AB_CH <= 256 and KVM * hd <= 256.
+template <typename T, int KVM>
+__global__ void __launch_bounds__(ATTN_THREADS) attn_batch_kernel(const AttnArgs a) {
+    static_assert(KVM >= 1 && KVM * AB_CH <= ATTN_THREADS, "attn_batch_kernel: KVM * AB_CH <= 256");
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(16) float qs[256 * KVM];   // [hd][KVM]
+    __shared__ float red[ATTN_THREADS / 32];
+    __shared__ float s_inv[KVM];
+    __shared__ double tab_s[64];
+    const int kvh = blockIdx.x, bt = blockIdx.y, tid = threadIdx.x, hd = a.hd;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int pos = a.bpos[bt], npos = pos + 1;
+    const int astr = a.ctx;   // scores row stride (positions)
+    const size_t coff = (size_t)bt * a.cache_stride;
+    const T *kt = reinterpret_cast<const T *>(a.kc) + coff + (size_t)kvh * hd * a.kstride;
+    const T *vt = reinterpret_cast<const T *>(a.vc) + coff + (size_t)kvh * a.ctx * hd;
+    T *buf0 = reinterpret_cast<T *>(smem);
+    const size_t cbuf = (size_t)AB_CH * hd;
+    float *att = reinterpret_cast<float *>(smem + 2 * cbuf * sizeof(T));
+    const int nch = (npos + AB_CH - 1) / AB_CH;
+    ab_stage_k(buf0, kt, a.kstride, 0, min(AB_CH, npos), hd);
+    expf_table_load(tab_s, a.ex);
+    for (int idx = tid; idx < KVM * hd; idx += ATTN_THREADS) {
+        const int hh = idx / hd, i = idx - hh * hd;
+        qs[i * KVM + hh] = a.q[(size_t)bt * a.nh * hd + (size_t)(kvh * KVM + hh) * hd + i];
+    }
+
+    // ---- scores: thread (tl, hs) = (position in the chunk, head) ----
+    const int tl = tid % AB_CH, hs = tid / AB_CH;
+    const float inv_sqrt = fdiv(1.0f, fsqrt((float)hd));
+    float lmax = -INFINITY;
+    for (int c = 0; c < nch; c++) {
+        const int c0 = c * AB_CH, n = min(AB_CH, npos - c0);
+        if (c + 1 < nch) {
+            ab_stage_k(buf0 + ((c + 1) & 1) * cbuf, kt, a.kstride, c0 + AB_CH, min(AB_CH, npos - c0 - AB_CH), hd);
+            cp_async_wait_1();
+        } else {
+            cp_async_wait_all();
+        }
+        __syncthreads();
+        const T *kb = buf0 + (c & 1) * cbuf;
+        if (hs < KVM && tl < n) {
+            float sc = 0.0f;
+            for (int i = 0; i < hd; i += 8) {
+                float kk[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) kk[j] = widen(kb[(size_t)(i + j) * AB_CH + tl]);
+#pragma unroll
+                for (int j = 0; j < 8; j++) sc = fadd(sc, fmul(qs[(i + j) * KVM + hs], kk[j]));
+            }
+            const float v = fmul(sc, inv_sqrt);
+            att[(size_t)hs * astr + c0 + tl] = v;
+            lmax = fmaxf(lmax, v);
+        }
+        __syncthreads();   // the buffer is free for chunk c + 2
+    }
+    // the first value chunk streams in during the softmax
+    ab_stage_v(buf0, vt, 0, min(AB_CH, npos), hd);
+
+    // ---- softmax per head (ref src/model.c:57-64) ----
+    // warp w holds positions of head (32 w) / AB_CH: AB_CH / 32 warps per head
+    lmax = warp_max(lmax);
+    if (lane == 0) red[warp] = lmax;
+    __syncthreads();
+    float mx[KVM];
+#pragma unroll
+    for (int hh = 0; hh < KVM; hh++) {
+        mx[hh] = red[hh * (AB_CH / 32)];
+#pragma unroll
+        for (int w = 1; w < AB_CH / 32; w++) mx[hh] = fmaxf(mx[hh], red[hh * (AB_CH / 32) + w]);
+    }
+#pragma unroll
+    for (int hh = 0; hh < KVM; hh++)
+        for (int t = tid; t < npos; t += ATTN_THREADS)
+            att[(size_t)hh * astr + t] = expf_exact(a.ex, tab_s, fsub(att[(size_t)hh * astr + t], mx[hh]));
+    __syncthreads();
+    // the denominators: the sequential sum over t = 0..pos, one lane per head
+    if (lane == 0 && warp < KVM) s_inv[warp] = fdiv(1.0f, chain_sum_pipe(0.0f, att + (size_t)warp * astr, npos));
+    __syncthreads();
+#pragma unroll
+    for (int hh = 0; hh < KVM; hh++)
+        for (int t = tid; t < npos; t += ATTN_THREADS) att[(size_t)hh * astr + t] = fmul(att[(size_t)hh * astr + t], s_inv[hh]);
+
+    // ---- out_i = sum_t w_t * v_t,i, sequential over t (ref src/model.c:252-256) ----
+    const int ho = tid / hd, io = tid - ho * hd;
+    const bool live = ho < KVM;
+    const float *w = att + (size_t)(live ? ho : 0) * astr;
+    float o = 0.0f;
+    for (int c = 0; c < nch; c++) {
+        const int c0 = c * AB_CH, n = min(AB_CH, npos - c0);
+        if (c + 1 < nch) {
+            ab_stage_v(buf0 + ((c + 1) & 1) * cbuf, vt, c0 + AB_CH, min(AB_CH, npos - c0 - AB_CH), hd);
+            cp_async_wait_1();
+        } else {
+            cp_async_wait_all();
+        }
+        __syncthreads();   // the chunk (and, for c = 0, the weights) are visible
+        const T *vb = buf0 + (c & 1) * cbuf;
+        if (live) {
+            int t = 0;
+            for (; t + 8 <= n; t += 8) {
+                float ww[8], vv[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) { ww[j] = w[c0 + t + j]; vv[j] = widen(vb[(size_t)(t + j) * hd + io]); }
+#pragma unroll
+                for (int j = 0; j < 8; j++) o = fadd(o, fmul(ww[j], vv[j]));
+            }
+            for (; t < n; t++) o = fadd(o, fmul(w[c0 + t], widen(vb[(size_t)t * hd + io])));
+        }
+        __syncthreads();   // the buffer is free for chunk c + 2
+    }
+    if (live) {
+        const int gi = (kvh * KVM + ho) * hd + io;
+        float dq;
+        const int8_t q = quant_lane(o, &dq);   // hd % 32 == 0: a warp holds one block of one head
+        a.bxq[(size_t)bt * a.k_pad + gi] = q;
+        if (lane == 0) a.bxs[(size_t)(gi / 32) * a.n_pad + bt] = dq;
+    }
+}
+
 }  // namespace emb

@@ -143,6 +143,12 @@ static int pf_init(int device) {
     if (pf_allow_smem(attn_decode_kernel<float, true>, optin - (int)fa.sharedSizeBytes)) return 1;
     CK(cudaFuncGetAttributes(&fa, attn_decode_kernel<__half, true>));
     if (pf_allow_smem(attn_decode_kernel<__half, true>, optin - (int)fa.sharedSizeBytes)) return 1;
+#define EMB_AB_ALLOW(T, K)                                                                    \
+    CK(cudaFuncGetAttributes(&fa, attn_batch_kernel<T, K>));                                  \
+    if (pf_allow_smem(attn_batch_kernel<T, K>, optin - (int)fa.sharedSizeBytes)) return 1;
+    EMB_AB_ALLOW(float, 1) EMB_AB_ALLOW(float, 2) EMB_AB_ALLOW(float, 3) EMB_AB_ALLOW(float, 4)
+    EMB_AB_ALLOW(__half, 1) EMB_AB_ALLOW(__half, 2) EMB_AB_ALLOW(__half, 3) EMB_AB_ALLOW(__half, 4)
+#undef EMB_AB_ALLOW
     if (device < 32) done |= 1u << device;
     return 0;
 }
@@ -522,9 +528,25 @@ static int pf_layers(EmberCudaModel *m, PfState *ps, const PfSeq &q, const int *
             da.att_in_smem = 1; da.chunk = q.dec_chunk; da.ex = m->ex;
             da.bpos = q.pos; da.cache_stride = q.cache_stride;
             da.bxq = ps->XQ; da.bxs = ps->XS; da.k_pad = ps->k_pad[PF_K_QD]; da.n_pad = ps->n_pad;
-            const dim3 dgrid((unsigned)m->n_heads, (unsigned)nc);
-            if (q.kv_fp16) attn_decode_kernel<__half, true><<<dgrid, ATTN_THREADS, q.dec_smem, st>>>(da);
-            else attn_decode_kernel<float, true><<<dgrid, ATTN_THREADS, q.dec_smem, st>>>(da);
+            const int kvm = m->n_heads / m->n_kv;
+            if (q.dec_attn == 1 && kvm <= 4 && kvm * hd <= ATTN_THREADS) {
+                // one CTA per (kv head, stream): its query heads share each staged chunk
+                const dim3 bgrid((unsigned)m->n_kv, (unsigned)nc);
+                const size_t bsm = ab_smem_bytes(hd, (int)es, kvm, q.ctx);
+#define EMB_AB(T)                                                                                   \
+    switch (kvm) {                                                                                  \
+    case 1: attn_batch_kernel<T, 1><<<bgrid, ATTN_THREADS, bsm, st>>>(da); break;                    \
+    case 2: attn_batch_kernel<T, 2><<<bgrid, ATTN_THREADS, bsm, st>>>(da); break;                    \
+    case 3: attn_batch_kernel<T, 3><<<bgrid, ATTN_THREADS, bsm, st>>>(da); break;                    \
+    default: attn_batch_kernel<T, 4><<<bgrid, ATTN_THREADS, bsm, st>>>(da); break;                   \
+    }
+                if (q.kv_fp16) { EMB_AB(__half) } else { EMB_AB(float) }
+#undef EMB_AB
+            } else {
+                const dim3 dgrid((unsigned)m->n_heads, (unsigned)nc);
+                if (q.kv_fp16) attn_decode_kernel<__half, true><<<dgrid, ATTN_THREADS, q.dec_smem, st>>>(da);
+                else attn_decode_kernel<float, true><<<dgrid, ATTN_THREADS, q.dec_smem, st>>>(da);
+            }
         } else {
             if (launch_pf_attn(q.kv_fp16 != 0, q.rs, pf_attn_rows_per_group(q.rs, hd), agrid, asmem, st, aa)) return 1;
         }
@@ -853,11 +875,14 @@ static int batch_record(EmberCudaBatch *b) {
     q.p_cap = (int)round_up((size_t)b->ctx, 4);
     q.tq = 1;
     q.rs = (m->n_heads / m->n_kv + 3) / 4 * 4;
-    // attention per (query head, stream) with the cache staged through shared
-    // memory (attn_decode_kernel); EMBER_BATCH_ATTN=tile keeps the token-tile
-    // kernel of the prefill (for comparisons)
+    // attention per (kv head, stream) (attn_batch_kernel) where the kv head's query
+    // heads fit one CTA, else per (query head, stream) (attn_decode_kernel, BATCH);
+    // EMBER_BATCH_ATTN=head forces the latter, =tile the prefill's token-tile
+    // kernel (for comparisons)
     const char *ba = getenv("EMBER_BATCH_ATTN");
-    q.dec_attn = w->att_in_smem && w->m->head_dim <= ATTN_THREADS && !(ba && strcmp(ba, "tile") == 0);
+    q.dec_attn = !(w->att_in_smem && w->m->head_dim <= ATTN_THREADS) || (ba && strcmp(ba, "tile") == 0)
+                     ? 0
+                     : ((ba && strcmp(ba, "head") == 0) ? 2 : 1);
     // chunks of 48 positions (fp32, head_dim 128: 48 KB of buffers), so several
     // (head, stream) CTAs share an SM; EMBER_BATCH_ATTN_CHUNK overrides (tuning)
     {

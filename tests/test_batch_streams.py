@@ -53,21 +53,22 @@ def run_batch(path, prompts, n_steps, kv16, ctx):
     return firsts, toks, logits
 
 
-@pytest.mark.parametrize("mode", ["replicas", "gemm", "gemm-tile", "gemm-swap"])
+@pytest.mark.parametrize("mode", ["replicas", "gemm", "gemm-head", "gemm-tile", "gemm-swap"])
 @pytest.mark.parametrize("kv16", [0, 1])
 @pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen3", "tiny-qwen2", "tiny-smol-q4", "tiny-mqa"])
 def test_tiny_streams_match_single_sequence_runs(orc, name, kv16, mode, monkeypatch):
     """five streams with prompts of 1..30 tokens, 12 steps together; up to 8
     streams run as concurrent single-stream states unless EMBER_BATCH=gemm
-    forces the batched GEMM path, whose attention runs per (head, stream)
-    (attn_decode_kernel) or, with EMBER_BATCH_ATTN=tile, as the prefill's
-    token-tile kernel, and whose GEMMs may swap operands (EMBER_PF_SWAP=1)"""
+    forces the batched GEMM path, whose attention runs per (kv head, stream)
+    (attn_batch_kernel), per (query head, stream) with EMBER_BATCH_ATTN=head
+    (attn_decode_kernel) or, with =tile, as the prefill's token-tile kernel, and
+    whose GEMMs may swap operands (EMBER_PF_SWAP=1)"""
     if mode.startswith("gemm"):
         monkeypatch.setenv("EMBER_BATCH", "gemm")
     else:
         monkeypatch.delenv("EMBER_BATCH", raising=False)
-    if mode == "gemm-tile":
-        monkeypatch.setenv("EMBER_BATCH_ATTN", "tile")
+    if mode in ("gemm-tile", "gemm-head"):
+        monkeypatch.setenv("EMBER_BATCH_ATTN", mode[5:])
     else:
         monkeypatch.delenv("EMBER_BATCH_ATTN", raising=False)
     if mode == "gemm-swap":   # the opt-in swapped-operand GEMM
