@@ -99,6 +99,16 @@ EMB_DEV int dot_q8_block(const uint8_t *w, const int8_t *xq) {
     return acc;
 }
 
+// int8 dot of 32 weight bytes (two int4) with 32 activation bytes, exact in int32
+EMB_DEV int dp8(int4 w0, int4 w1, int4 a0, int4 a1) {
+    int acc = 0;
+    acc = __dp4a(w0.x, a0.x, acc); acc = __dp4a(w0.y, a0.y, acc);
+    acc = __dp4a(w0.z, a0.z, acc); acc = __dp4a(w0.w, a0.w, acc);
+    acc = __dp4a(w1.x, a1.x, acc); acc = __dp4a(w1.y, a1.y, acc);
+    acc = __dp4a(w1.z, a1.z, acc); acc = __dp4a(w1.w, a1.w, acc);
+    return acc;
+}
+
 // Q4_0 block (16 B): element i is nibble (byte i & 15) - 8, element i+16 is
 // (byte i >> 4) - 8 (ref src/kernels.c:175-179). Unsigned nibbles fit in a
 // signed byte, so sum((n-8)*a) = sum(n*a) - 8*sum(a), all exact in int32.

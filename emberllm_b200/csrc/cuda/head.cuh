@@ -89,15 +89,6 @@ EMB_DEV void head_issue(const HeadArgs &a, int g, unsigned char *dst, uint64_t *
     bulk_g2s(dst + head_q_bytes(Q4, a.cols), a.s + (size_t)row0 * nb, sb, bar);
 }
 
-EMB_DEV int dp8(int4 w0, int4 w1, int4 a0, int4 a1) {
-    int acc = 0;
-    acc = __dp4a(w0.x, a0.x, acc); acc = __dp4a(w0.y, a0.y, acc);
-    acc = __dp4a(w0.z, a0.z, acc); acc = __dp4a(w0.w, a0.w, acc);
-    acc = __dp4a(w1.x, a1.x, acc); acc = __dp4a(w1.y, a1.y, acc);
-    acc = __dp4a(w1.z, a1.z, acc); acc = __dp4a(w1.w, a1.w, acc);
-    return acc;
-}
-
 template <bool ARGMAX, bool Q4>
 __global__ void __launch_bounds__(HEAD_THREADS, 1) lm_head_kernel(const HeadArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];

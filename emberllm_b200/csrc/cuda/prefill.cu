@@ -99,6 +99,7 @@ static int pf_allow_smem(K kernel, int bytes) {
 }
 
 static int g_att_smem_cap = 0;   // dynamic smem the attention kernel may use
+static int g_mtv_smem_cap = 0;   // dynamic smem the multi-token GEMV may use
 
 static int pf_init(int device) {
     static unsigned done = 0;
@@ -137,8 +138,19 @@ static int pf_init(int device) {
 #undef EMB_ALLOW
 #undef EMB_PF_ATT_EACH
     g_att_smem_cap = cap;
-    // the batched decode attention (attn_decode_kernel, BATCH mode)
+    // the multi-token GEMV
     cudaFuncAttributes fa;
+    {
+        CK(cudaFuncGetAttributes(&fa, pf_mtv_kernel<PF_EPI_STORE>));
+        const int c1 = optin - (int)fa.sharedSizeBytes;
+        CK(cudaFuncGetAttributes(&fa, pf_mtv_kernel<PF_EPI_RESID>));
+        const int c2 = optin - (int)fa.sharedSizeBytes;
+        g_mtv_smem_cap = c1 < c2 ? c1 : c2;
+        if (pf_allow_smem(pf_mtv_kernel<PF_EPI_STORE>, g_mtv_smem_cap) ||
+            pf_allow_smem(pf_mtv_kernel<PF_EPI_RESID>, g_mtv_smem_cap))
+            return 1;
+    }
+    // the batched decode attention (attn_decode_kernel, BATCH mode)
     CK(cudaFuncGetAttributes(&fa, attn_decode_kernel<float, true>));
     if (pf_allow_smem(attn_decode_kernel<float, true>, optin - (int)fa.sharedSizeBytes)) return 1;
     CK(cudaFuncGetAttributes(&fa, attn_decode_kernel<__half, true>));
@@ -391,8 +403,43 @@ static int launch_gemm_bn(const PfMat &w, const CUtensorMap &mb, const PfGemmArg
     return 0;
 }
 
-static int launch_gemm(const PfMat &w, const CUtensorMap (&maps)[PF_NBN], const float *xs, int n_pad, int n,
-                       float *out, int ld, bool resid, int *err, int n_sm, cudaStream_t st) {
+// Few tokens: the dp4a multi-token GEMV. It wins on the short, long-K residual
+// matrices (wo, w2: a tensor-core CTA walks 64-96 serial block MMAs) up to 64
+// tokens, on the others only up to 16 (Qwen3 streams, measured: 16 streams 4.8k ->
+// 6.7k tok/s; 32 streams best without it on q|k|v and w1|w3; 64 streams 14.7k ->
+// 17.1k), and never on the vocabulary-sized head. EMBER_PF_MTV=0 disables it,
+// EMBER_PF_MTV_STORE sets the second count (tuning).
+static bool use_mtv(int n, bool resid, int rows) {
+    static int cap = -1, cap_store = -1;
+    if (cap < 0) {
+        const char *e = getenv("EMBER_PF_MTV");
+        cap = e && *e && atoi(e) == 0 ? 0 : 64;
+        const char *f = getenv("EMBER_PF_MTV_STORE");
+        cap_store = f && *f ? atoi(f) : 16;
+        if (cap_store > cap) cap_store = cap;
+    }
+    if (rows > 16384) return false;
+    return n <= (resid ? cap : cap_store);
+}
+
+template <int EPI>
+static int launch_mtv(const PfMat &w, const int8_t *xq, const float *xs, int n_pad, int n, float *out, int ld,
+                      int *err, cudaStream_t st) {
+    PfMtvArgs a;
+    a.wq = w.q; a.ws = w.s; a.xq = xq; a.xs = xs; a.out = out; a.err = err;
+    a.rows = w.rows; a.nb = w.nb; a.nbp = w.nbp; a.k_pad = w.k_pad; a.n = n; a.n_pad = n_pad; a.ld = ld;
+    const size_t sm = mtv_smem_bytes(w.k_pad, w.nbp);
+    dim3 grid((unsigned)(w.rows_pad / MTV_R), (unsigned)((n + MTV_T - 1) / MTV_T));
+    pf_mtv_kernel<EPI><<<grid, MTV_R * MTV_T, sm, st>>>(a);
+    CK(cudaGetLastError());
+    return 0;
+}
+
+static int launch_gemm(const PfMat &w, const CUtensorMap (&maps)[PF_NBN], const int8_t *xq, const float *xs,
+                       int n_pad, int n, float *out, int ld, bool resid, int *err, int n_sm, cudaStream_t st) {
+    if (xq && use_mtv(n, resid, w.rows) && mtv_smem_bytes(w.k_pad, w.nbp) <= (size_t)g_mtv_smem_cap)
+        return resid ? launch_mtv<PF_EPI_RESID>(w, xq, xs, n_pad, n, out, ld, err, st)
+                     : launch_mtv<PF_EPI_STORE>(w, xq, xs, n_pad, n, out, ld, err, st);
     PfGemmArgs a;
     a.ws = w.s; a.ws_t = w.s_t; a.rows_pad = w.rows_pad; a.xs = xs; a.out = out; a.err = err;
     a.rows = w.rows; a.nb = w.nb; a.nbp = w.nbp; a.n = n; a.n_pad = n_pad; a.ld = ld;
@@ -498,7 +545,7 @@ static int pf_layers(EmberCudaModel *m, PfState *ps, const PfSeq &q, const int *
         ta.x = ps->X; ta.ld_x = m->dim; ta.norm_w = L.attn_norm; ta.cols = m->dim; ta.k_pad = ps->k_pad[PF_K_DIM];
         pf_norm_quant_kernel<<<nc, 256, (size_t)m->dim * 8, st>>>(ta);
         CK(cudaGetLastError());
-        if (launch_gemm(P.qkv, ps->mapB[PF_K_DIM], ps->XS, ps->n_pad, nc, ps->QKV, ps->ld_qkv, false, err, m->n_sm, st))
+        if (launch_gemm(P.qkv, ps->mapB[PF_K_DIM], ps->XQ, ps->XS, ps->n_pad, nc, ps->QKV, ps->ld_qkv, false, err, m->n_sm, st))
             return 1;
         PfQkvArgs qa;
         qa.qkv = ps->QKV; qa.ld = ps->ld_qkv; qa.bq = L.bq; qa.bk = L.bk; qa.bv = L.bv;
@@ -551,19 +598,19 @@ static int pf_layers(EmberCudaModel *m, PfState *ps, const PfSeq &q, const int *
             if (launch_pf_attn(q.kv_fp16 != 0, q.rs, pf_attn_rows_per_group(q.rs, hd), agrid, asmem, st, aa)) return 1;
         }
         CK(cudaGetLastError());
-        if (launch_gemm(P.wo, ps->mapB[PF_K_QD], ps->XS, ps->n_pad, nc, ps->X, m->dim, true, err, m->n_sm, st))
+        if (launch_gemm(P.wo, ps->mapB[PF_K_QD], ps->XQ, ps->XS, ps->n_pad, nc, ps->X, m->dim, true, err, m->n_sm, st))
             return 1;
         // feed-forward block
         ta.x = ps->X; ta.ld_x = m->dim; ta.norm_w = L.ffn_norm; ta.cols = m->dim; ta.k_pad = ps->k_pad[PF_K_DIM];
         pf_norm_quant_kernel<<<nc, 256, (size_t)m->dim * 8, st>>>(ta);
         CK(cudaGetLastError());
-        if (launch_gemm(P.w13, ps->mapB[PF_K_DIM], ps->XS, ps->n_pad, nc, ps->H, ps->ld_h, false, err, m->n_sm, st))
+        if (launch_gemm(P.w13, ps->mapB[PF_K_DIM], ps->XQ, ps->XS, ps->n_pad, nc, ps->H, ps->ld_h, false, err, m->n_sm, st))
             return 1;
         ta.x = ps->H; ta.ld_x = ps->ld_h; ta.norm_w = nullptr; ta.cols = m->hidden; ta.hidden = m->hidden;
         ta.k_pad = ps->k_pad[PF_K_HID];
         pf_swiglu_quant_kernel<<<nc, 256, (size_t)m->hidden * 4, st>>>(ta);
         CK(cudaGetLastError());
-        if (launch_gemm(P.w2, ps->mapB[PF_K_HID], ps->XS, ps->n_pad, nc, ps->X, m->dim, true, err, m->n_sm, st))
+        if (launch_gemm(P.w2, ps->mapB[PF_K_HID], ps->XQ, ps->XS, ps->n_pad, nc, ps->X, m->dim, true, err, m->n_sm, st))
             return 1;
     }
     return 0;
@@ -633,7 +680,7 @@ int pf_matmul_batch(int device, float *out, const float *x, const DevMat &w, int
         pf_quant_kernel<<<B, 256, (size_t)w.cols * 4>>>(ta);
         if (cudaGetLastError() != cudaSuccess) rc = set_err("pf_matmul_batch: quant launch failed");
     }
-    if (!rc) rc = launch_gemm(pk, maps, dxs, n_pad, B, dout, w.rows, false, derr, nsm, 0);
+    if (!rc) rc = launch_gemm(pk, maps, dxq, dxs, n_pad, B, dout, w.rows, false, derr, nsm, 0);
     int herr = 0;
     if (!rc && (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpy(&herr, derr, 4, cudaMemcpyDeviceToHost) != cudaSuccess))
         rc = set_err("pf_matmul_batch: %s", cudaGetErrorString(cudaGetLastError()));
@@ -904,7 +951,7 @@ static int batch_record(EmberCudaBatch *b) {
     ta.x = ps->X; ta.ld_x = m->dim; ta.norm_w = m->final_norm; ta.cols = m->dim; ta.k_pad = ps->k_pad[PF_K_DIM];
     pf_norm_quant_kernel<<<b->S, 256, (size_t)m->dim * 8, st>>>(ta);
     CK(cudaGetLastError());
-    if (launch_gemm(m->pf->head, ps->mapB[PF_K_DIM], ps->XS, ps->n_pad, b->S, b->logits, b->ld_log, false, err,
+    if (launch_gemm(m->pf->head, ps->mapB[PF_K_DIM], ps->XQ, ps->XS, ps->n_pad, b->S, b->logits, b->ld_log, false, err,
                     m->n_sm, st))
         return 1;
     batch_argmax_kernel<<<b->S, 256, 0, st>>>(b->logits, b->ld_log, m->vocab, b->tok, b->pos, b->out, b->nout, b->S);

@@ -494,6 +494,74 @@ __global__ void __launch_bounds__(PfLayout<BN>::THREADS, PfLayout<BN>::MIN_CTAS)
     PF_CTA_MARK(2);
 }
 
+// --------------------------------------------------- few tokens: dp4a GEMV -------
+// A multi-token GEMV for batches of at most a few dozen tokens (batched decode
+// of streams, short prefills), where the tensor-core tiles leave a CTA walking
+// a long serial chain of block MMAs. One CTA per (16 weight rows, 16 tokens):
+// bulk copies bring the rows (int8, the pack's layout), their fp32 scales and
+// the tokens' int8 activations (rows padded by 16 bytes, so the eight threads
+// of a shared-memory phase read eight bank groups); thread (row, token) runs
+// that output's chain: per block the int32 dot (exact), the term
+// ((float)acc * d_w) * d_x, added in block order (ref src/kernels.c:152-164).
+constexpr int MTV_R = 16, MTV_T = 16;
+
+struct PfMtvArgs {
+    const int8_t *wq;    // pack rows [rows_pad][k_pad]
+    const float *ws;     // pack scales [rows_pad][nbp]
+    const int8_t *xq;    // activations [n_pad][k_pad]
+    const float *xs;     // activation scales [nb][n_pad]
+    float *out;          // STORE: out[t*ld + r] = y; RESID: += y
+    int *err;
+    int rows, nb, nbp, k_pad, n, n_pad, ld;
+};
+
+__host__ __device__ inline size_t mtv_smem_bytes(int k_pad, int nbp) {
+    return (size_t)MTV_R * k_pad + (size_t)MTV_T * (k_pad + 16) + (size_t)MTV_R * nbp * 4 + (size_t)nbp * MTV_T * 4;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(MTV_R * MTV_T) pf_mtv_kernel(const PfMtvArgs a) {
+    extern __shared__ __align__(128) unsigned char mtv_sm[];
+    __shared__ __align__(8) uint64_t bar;
+    const int tid = threadIdx.x, r0 = blockIdx.x * MTV_R, t0 = blockIdx.y * MTV_T;
+    const int nt = min(MTV_T, a.n - t0), kp = a.k_pad, xstride = kp + 16;
+    int8_t *wq_s = reinterpret_cast<int8_t *>(mtv_sm);                    // [MTV_R][kp]
+    int8_t *xq_s = wq_s + (size_t)MTV_R * kp;                              // [MTV_T][kp + 16]
+    float *ws_s = reinterpret_cast<float *>(xq_s + (size_t)MTV_T * xstride);   // [MTV_R][nbp]
+    float *xs_s = ws_s + (size_t)MTV_R * a.nbp;                           // [nbp][MTV_T]
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_expect_tx(&bar, (uint32_t)(MTV_R * kp + MTV_R * a.nbp * 4 + nt * kp));
+        bulk_g2s(wq_s, a.wq + (size_t)r0 * kp, (uint32_t)(MTV_R * kp), &bar);
+        bulk_g2s(ws_s, a.ws + (size_t)r0 * a.nbp, (uint32_t)(MTV_R * a.nbp * 4), &bar);
+        for (int t = 0; t < nt; t++)
+            bulk_g2s(xq_s + (size_t)t * xstride, a.xq + (size_t)(t0 + t) * kp, (uint32_t)kp, &bar);
+    }
+    // the activation scales of these tokens (n_pad >= t0 + MTV_T: in bounds)
+    for (int idx = tid; idx < a.nb * MTV_T; idx += MTV_R * MTV_T) {
+        const int b = idx / MTV_T, t = idx - b * MTV_T;
+        xs_s[idx] = a.xs[(size_t)b * a.n_pad + t0 + t];
+    }
+    __syncthreads();
+    mbar_wait_cta(&bar, 0, a.err, ERR_PF_WAIT);
+    const int r = tid / MTV_T, t = tid - r * MTV_T, row = r0 + r;
+    if (t < nt && row < a.rows) {
+        const int8_t *wr = wq_s + (size_t)r * kp, *xr = xq_s + (size_t)t * xstride;
+        const float *wsr = ws_s + (size_t)r * a.nbp, *xsr = xs_s + t;
+        float s = 0.0f;
+#pragma unroll 4
+        for (int b = 0; b < a.nb; b++) {
+            const int4 *wv = reinterpret_cast<const int4 *>(wr + b * 32);
+            const int4 *xv = reinterpret_cast<const int4 *>(xr + b * 32);
+            const int acc = dp8(wv[0], wv[1], xv[0], xv[1]);
+            s = fadd(s, fmul(fmul(__int2float_rn(acc), wsr[b]), xsr[b * MTV_T]));
+        }
+        float *o = a.out + (size_t)(t0 + t) * a.ld + row;
+        *o = EPI == PF_EPI_RESID ? fadd(*o, s) : s;
+    }
+}
+
 // --------------------------------------------------------------- packing -------
 
 // dst[b][r] = src[r][b] for a [rows][cols] fp32 matrix (the weight scales'
