@@ -407,13 +407,14 @@ static int launch_gemm_bn(const PfMat &w, const CUtensorMap &mb, const PfGemmArg
 // matrices (wo, w2: a tensor-core CTA walks 64-96 serial block MMAs) up to 64
 // tokens, on the others only up to 16 (Qwen3 streams, measured: 16 streams 4.8k ->
 // 6.7k tok/s; 32 streams best without it on q|k|v and w1|w3; 64 streams 14.7k ->
-// 17.1k), and never on the vocabulary-sized head. EMBER_PF_MTV=0 disables it,
-// EMBER_PF_MTV_STORE sets the second count (tuning).
+// 17.1k), and never on the vocabulary-sized head. EMBER_PF_MTV sets the first
+// count (0 disables it), EMBER_PF_MTV_STORE the second (tuning).
 static bool use_mtv(int n, bool resid, int rows) {
     static int cap = -1, cap_store = -1;
     if (cap < 0) {
         const char *e = getenv("EMBER_PF_MTV");
-        cap = e && *e && atoi(e) == 0 ? 0 : 64;
+        cap = e && *e ? atoi(e) : 64;
+        if (cap < 0) cap = 0;
         const char *f = getenv("EMBER_PF_MTV_STORE");
         cap_store = f && *f ? atoi(f) : 16;
         if (cap_store > cap) cap_store = cap;
@@ -461,12 +462,17 @@ static int launch_gemm(const PfMat &w, const CUtensorMap (&maps)[PF_NBN], const 
     }
 }
 
-// attention tile: tokens per CTA so that rows * positions fit shared memory
-// attention tile: the most tokens per CTA (rows = tokens x kv_mul <= 16) whose
-// weights [positions][rows rounded up to 4] fit shared memory; 0 if none does
+// attention tile: the most tokens per CTA (rows = tokens x kv_mul <= 16 at
+// head_dim 128, <= 8 at head_dim 64 and below, where the shorter chains favour
+// more, smaller CTAs -- measured: SmolLM2 pp512 96k -> 105k tok/s, Qwen3 best at
+// 16; EMBER_PF_ATT_ROWS overrides, a tuning knob) whose weights [positions][rows
+// rounded up to 4] fit shared memory; 0 if none does
 static int attn_tile(const EmberCudaModel *m, int p_cap, int *tq, int *rs) {
     const int kv_mul = m->n_heads / m->n_kv;
-    for (int t = PF_ATT_MAX_ROWS / kv_mul; t > 0; t--) {
+    const char *rc = getenv("EMBER_PF_ATT_ROWS");
+    const int def_rows = m->head_dim <= 64 && kv_mul <= 8 ? 8 : PF_ATT_MAX_ROWS;
+    const int max_rows = rc && atoi(rc) >= kv_mul && atoi(rc) <= PF_ATT_MAX_ROWS ? atoi(rc) : def_rows;
+    for (int t = max_rows / kv_mul; t > 0; t--) {
         const int r = (t * kv_mul + 3) / 4 * 4;
         if (pf_attn_smem(p_cap, r, m->head_dim, 4) <= (size_t)g_att_smem_cap) {   // fp32 cache: the larger
             *tq = t;
