@@ -74,7 +74,7 @@ def test_synthetic_writer_equals_quantize_file_of_f32(libs, tmp_path):
     assert open(q, "rb").read() == open(direct, "rb").read()
 
 
-def test_weight_bytes_per_token_matches_survey_figures():
+def test_weight_bytes_per_token_matches_the_stated_figures():
     # algorithmic weight bytes per decoded token: stories110M 116.4 MB, Qwen3 633.5 MB
     s = synth.weight_bytes_per_token(synth.CONFIGS["stories110m"]) / 1e6
     q = synth.weight_bytes_per_token(synth.CONFIGS["qwen3-0.6b"]) / 1e6
