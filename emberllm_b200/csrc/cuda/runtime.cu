@@ -271,14 +271,17 @@ extern "C" int ember_cuda_state_new(EmberCudaModel *m, int ctx, int kv_fp16, con
     rc |= salloc(s, (void **)&s->v, (size_t)kvd * 4);
     // split attention (attn_split.cuh): AS_PER cached positions per scoring CTA;
     // the softmax weights sit in shared memory when they fit
-    // Short contexts keep the single-kernel attention (one launch fewer per layer;
-    // measured faster up to a few hundred positions); longer ones split the cache
-    // over CTAs. EMBER_ATTN=fused / split forces one (for comparisons).
+    // Short contexts keep the single-kernel attention (one launch fewer per layer);
+    // longer ones split the cache over CTAs. The crossover scales with the work per
+    // position: 512 positions at head_dim 128 (Qwen3 at 1160: split 721 tok/s, fused
+    // 563), 1024 at head_dim 64 and below (Qwen2.5 at 648: fused 987 against 723;
+    // SmolLM2 at 776: 937 against 870). EMBER_ATTN=fused / split forces one.
     const char *attn_env = getenv("EMBER_ATTN");
     const bool force_fused = attn_env && strcmp(attn_env, "fused") == 0;
     const bool force_split = attn_env && strcmp(attn_env, "split") == 0;
+    const int split_above = hd <= 64 ? 1024 : 512;
     s->attn_split = m->n_heads / m->n_kv <= AS_MAX_KVMUL && hd <= 256 && hd % 32 == 0 && !force_fused &&
-                    (force_split || ctx > 512);
+                    (force_split || ctx > split_above);
     s->attn_splits = (ctx + AS_PER - 1) / AS_PER;
     s->attn_w_smem = as_pv_smem(m->n_heads / m->n_kv, ctx, (int)es, 1) <= 200 * 1024;
     s->att_stride = (ctx + 63) / 64 * 64;   // split_chain_sum pads rows to 64 positions
