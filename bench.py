@@ -64,6 +64,9 @@ def parse():
     p.add_argument("--agg-streams", default="16,64",
                    help="with the headline: also decode 8 x N independent streams split over "
                         "the GPUs for each N listed (BASELINE configs[4]); '' or 0 skips")
+    p.add_argument("--agg-per-gpu", type=int, default=64,
+                   help="with the streams aggregate: also this many streams on every GPU "
+                        "(weak scaling); 0 skips")
     p.add_argument("--agg-tokens", type=int, default=64,
                    help="greedy tokens per stream per timed step of the streams aggregate")
     p.add_argument("--prefill-only", action="store_true",
@@ -573,12 +576,22 @@ def run_ours(args, world, rank, local, dist):
         "clocks": clk,
     }
     # BASELINE configs[4] beside the headline: 8 x 16 and 8 x 64 streams split
-    # over the N GPUs (the multi-GPU target; the headline stays single-stream)
+    # over the N GPUs (strong scaling), and 64 streams on every GPU (weak scaling);
+    # the headline stays single-stream
     aggs = []
     for n_per in [int(v) for v in args.agg_streams.split(",") if v.strip() and int(v) > 0]:
         total = 8 * n_per
         m = streams_measure(args, world, rank, local, dist, total, args.agg_tokens, 2, args.warmup)
-        aggs.append(streams_summary(m, total, world, args.agg_tokens, 2))
+        sm = streams_summary(m, total, world, args.agg_tokens, 2)
+        sm["scaling"] = "strong"
+        aggs.append(sm)
+    # and a fixed number of streams per GPU (weak scaling: 64 x N streams in all)
+    if args.agg_per_gpu > 0 and args.agg_streams.strip():
+        total = args.agg_per_gpu * world
+        m = streams_measure(args, world, rank, local, dist, total, args.agg_tokens, 2, args.warmup)
+        sm = streams_summary(m, total, world, args.agg_tokens, 2)
+        sm["scaling"] = "weak"
+        aggs.append(sm)
     if aggs:
         line["streams_aggregate"] = aggs
     if rank == 0 and world == 1 and args.cpu_baseline:
