@@ -206,6 +206,41 @@ __global__ void smp_bitonic_pass(unsigned long long *keys, int npow2, int k, int
 EMB_DEV float key_p(unsigned long long k) { return __uint_as_float(~(uint32_t)(k >> 32)); }
 EMB_DEV int key_i(unsigned long long k) { return (int)(uint32_t)(k & 0xFFFFFFFFu); }
 
+// The running sum over cand[0..cnt) continued from *sum, 16 candidates at a time:
+// the loads go out first, the additions form a clean dependent chain (entries
+// past cnt add +0, which leaves a non-negative sum unchanged), and the running
+// sums are tested afterwards. Returns the first index whose running sum meets
+// the test (top-p: sum >= lim; draw: lim < sum), with *sum the running sum
+// there, or -1 with *sum the sum of all cnt terms -- the reference's loops'
+// additions and stopping point exactly.
+template <bool DRAW>
+EMB_DEV int pick_walk(const unsigned long long *cand, int cnt, float lim, float *sum) {
+    float s = *sum;
+    for (int i0 = 0; i0 < cnt; i0 += 16) {
+        float pv[16], rs[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const float v = key_p(cand[i0 + j]);   // within the staged chunk
+            pv[j] = i0 + j < cnt ? v : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            s = fadd(s, pv[j]);
+            rs[j] = s;
+        }
+        int hit = -1;
+#pragma unroll
+        for (int j = 15; j >= 0; j--)
+            if (i0 + j < cnt && (DRAW ? lim < rs[j] : rs[j] >= lim)) hit = j;
+        if (hit >= 0) {
+            *sum = rs[hit];
+            return i0 + hit;
+        }
+    }
+    *sum = s;
+    return -1;
+}
+
 // The truncation and the draw over the sorted candidates (ref src/sample.c:
 // 139-172), thread 0 walking staged chunks of the sorted keys in order.
 __global__ void __launch_bounds__(SM_THREADS) smp_pick(const unsigned long long *keys, SampleArgs a, int *res_i) {
@@ -216,13 +251,23 @@ __global__ void __launch_bounds__(SM_THREADS) smp_pick(const unsigned long long 
     const int n = a.n;
     int m = n;
     if (a.top_k > 0 && a.top_k < m) m = a.top_k;
-    // min-p: the prefix with p >= min_p * p_max (short in practice: per element)
+    // min-p: the prefix with p >= min_p * p_max, 16 keys loaded ahead of the tests
     if (threadIdx.x == 0) {
         if (a.min_p > 0.0f && a.min_p < 1.0f) {
             const float thresh = fmul(a.min_p, key_p(keys[0]));
             int keep = 1;
-            while (keep < m && key_p(keys[keep]) >= thresh) keep++;
-            m = keep;
+            for (;;) {
+                float pv[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) pv[j] = keep + j < m ? key_p(keys[keep + j]) : -1.0f;
+                int pass = 16;
+#pragma unroll
+                for (int j = 15; j >= 0; j--)
+                    if (!(pv[j] >= thresh)) pass = j;   // the first candidate below the threshold
+                keep += pass;
+                if (pass < 16 || keep >= m) break;
+            }
+            m = keep < m ? keep : m;
         }
         s_m = m;
         s_done = 0;
@@ -239,9 +284,10 @@ __global__ void __launch_bounds__(SM_THREADS) smp_pick(const unsigned long long 
         for (int i = threadIdx.x; i < cnt; i += SM_THREADS) buf[0][i] = keys[base + i];
         __syncthreads();
         if (threadIdx.x == 0 && !s_done) {
-            for (int i = 0; i < cnt; i++) {
-                cum = fadd(cum, key_p(buf[0][i]));
-                if (top_p && cum >= a.top_p) { last = base + i; s_done = 1; break; }
+            const int hit = pick_walk<false>(buf[0], cnt, top_p ? a.top_p : INFINITY, &cum);
+            if (hit >= 0) {
+                last = base + hit;
+                s_done = 1;
             }
         }
         __syncthreads();
@@ -266,9 +312,10 @@ __global__ void __launch_bounds__(SM_THREADS) smp_pick(const unsigned long long 
         for (int i = threadIdx.x; i < cnt; i += SM_THREADS) buf[1][i] = keys[base + i];
         __syncthreads();
         if (threadIdx.x == 0 && !s_done) {
-            for (int i = 0; i < cnt; i++) {
-                run = fadd(run, key_p(buf[1][i]));
-                if (r < run) { chosen = key_i(buf[1][i]); s_done = 1; break; }
+            const int hit = pick_walk<true>(buf[1], cnt, r, &run);
+            if (hit >= 0) {
+                chosen = key_i(buf[1][hit]);
+                s_done = 1;
             }
         }
         __syncthreads();
