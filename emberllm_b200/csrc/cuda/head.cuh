@@ -128,17 +128,22 @@ __global__ void __launch_bounds__(HEAD_THREADS, 1) lm_head_kernel(const HeadArgs
     }
     __syncthreads();
     const float sc = rms_scale(split_chain_sum<HEAD_THREADS>(sq_s, cols), cols, a.eps);
-    for (int i = tid; i < cols; i += HEAD_THREADS) x_s[i] = fmul(fmul(x_s[i], sc), nw_s[i]);   // (x*scale)*w
-    __syncthreads();
-    // quantize (ref src/kernels.c:211): eight threads per 32-block, four elements each
+    // normalize (x*scale)*w and quantize (ref src/kernels.c:211): eight threads per
+    // 32-block, four elements each, each thread normalizing the four it quantizes
     for (int base = 0; base < nb * 8; base += HEAD_THREADS) {
         const int q8 = base + tid;
         const bool act = q8 < nb * 8;
         const unsigned mask = __ballot_sync(0xffffffffu, act);
         if (act) {
             const int b = q8 >> 3, sub = q8 & 7;
+            float4 v = reinterpret_cast<const float4 *>(x_s + b * 32)[sub];
+            const float4 w = reinterpret_cast<const float4 *>(nw_s + b * 32)[sub];
+            v.x = fmul(fmul(v.x, sc), w.x);
+            v.y = fmul(fmul(v.y, sc), w.y);
+            v.z = fmul(fmul(v.z, sc), w.z);
+            v.w = fmul(fmul(v.w, sc), w.w);
             float dq;
-            const uint32_t packed = quant_quad(reinterpret_cast<const float4 *>(x_s + b * 32)[sub], mask, &dq);
+            const uint32_t packed = quant_quad(v, mask, &dq);
             reinterpret_cast<uint32_t *>(xq_s + b * 32)[sub] = packed;
             if (sub == 0) xd_s[b] = dq;
         }

@@ -231,25 +231,36 @@ __global__ void __launch_bounds__(GEMV_THREADS) ember_q8_gemv_kernel(const GemvA
         } else {
             for (int i = tid; i < cols; i += GEMV_THREADS) xf_s[i] = a.x[i];
         }
+        // the split sum's barriers publish x and the squares; IN_RAW needs one here
+        float sc = 1.0f;
         if (IN == IN_NORM) {
             __syncthreads();
             EMB_PROBE(PK, 3);
-            const float sc = rms_scale(split_chain_sum<GEMV_THREADS>(sq_s, cols), cols, a.eps);
+            sc = rms_scale(split_chain_sum<GEMV_THREADS>(sq_s, cols), cols, a.eps);
             EMB_PROBE(PK, 4);
-            for (int i = tid; i < cols; i += GEMV_THREADS)
-                xf_s[i] = fmul(fmul(xf_s[i], sc), nw_s[i]);   // (x*scale)*w
+        } else {
+            __syncthreads();
         }
-        __syncthreads();
-        // quantize the activation (ref src/kernels.c:211): eight threads per
-        // 32-block, four elements each, every block at once
+        // normalize (x*scale)*w and quantize the activation (ref src/kernels.c:211):
+        // eight threads per 32-block, four elements each (each thread normalizes
+        // the four it quantizes), every block at once
         for (int base = 0; base < nb * 8; base += GEMV_THREADS) {
             const int q8 = base + tid;
             const bool act = q8 < nb * 8;
             const unsigned mask = __ballot_sync(0xffffffffu, act);
             if (act) {
                 const int b = q8 >> 3, sub = q8 & 7;
+                float4 v = reinterpret_cast<const float4 *>(xf_s + b * 32)[sub];
+                if (IN == IN_NORM) {
+                    const float4 w = reinterpret_cast<const float4 *>(nw_s + b * 32)[sub];
+                    v.x = fmul(fmul(v.x, sc), w.x);
+                    v.y = fmul(fmul(v.y, sc), w.y);
+                    v.z = fmul(fmul(v.z, sc), w.z);
+                    v.w = fmul(fmul(v.w, sc), w.w);
+                    reinterpret_cast<float4 *>(xf_s + b * 32)[sub] = v;   // the fp32 weights' path reads it
+                }
                 float dq;
-                const uint32_t packed = quant_quad(reinterpret_cast<const float4 *>(xf_s + b * 32)[sub], mask, &dq);
+                const uint32_t packed = quant_quad(v, mask, &dq);
                 reinterpret_cast<uint32_t *>(xq_s + b * 32)[sub] = packed;
                 if (sub == 0) xd_s[b] = dq;
                 if (IN == IN_RAW && blockIdx.x == 0 && a.xq_out) {
