@@ -140,28 +140,30 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
         __syncthreads();
         EMB_PROBE(4, 3);
         if (a.q_norm) {
-            // per-head RMSNorm of q and k, in place (ref src/model.c:386-389); the two
+            // per-head RMSNorm of q and k (ref src/model.c:386-389); the two
             // sequential sums run on different warps
             if (tid == 0) s_q = rms_scale(chain_sumsq(qs, hd), hd, a.eps);
             else if (tid == 32) s_k = rms_scale(chain_sumsq(ks, hd), hd, a.eps);
             __syncthreads();
-            if (tid < hd) {
-                qs[tid] = fmul(fmul(qs[tid], s_q), qn_s[tid]);
-                ks[tid] = fmul(fmul(ks[tid], s_k), kn_s[tid]);
-            }
-            __syncthreads();
         }
         EMB_PROBE(4, 4);
-        // RoPE (ref src/model.c:66-80) with the host-built cos/sin table
+        // RoPE (ref src/model.c:66-80) with the host-built cos/sin table; the
+        // thread that rotates a pair first applies the QK-norm scale and weights
+        // to it, (v*scale)*w, in registers
         if (tid < hd / 2) {
             const int ia = a.neox ? tid : 2 * tid, ib = a.neox ? tid + hd / 2 : 2 * tid + 1;
             const float2 cs = cs_s[tid];
-            float v0 = qs[ia], v1 = qs[ib];
-            qs[ia] = fsub(fmul(v0, cs.x), fmul(v1, cs.y));
-            qs[ib] = fadd(fmul(v0, cs.y), fmul(v1, cs.x));
-            v0 = ks[ia]; v1 = ks[ib];
-            ks[ia] = fsub(fmul(v0, cs.x), fmul(v1, cs.y));
-            ks[ib] = fadd(fmul(v0, cs.y), fmul(v1, cs.x));
+            float q0 = qs[ia], q1 = qs[ib], k0 = ks[ia], k1 = ks[ib];
+            if (a.q_norm) {
+                q0 = fmul(fmul(q0, s_q), qn_s[ia]);
+                q1 = fmul(fmul(q1, s_q), qn_s[ib]);
+                k0 = fmul(fmul(k0, s_k), kn_s[ia]);
+                k1 = fmul(fmul(k1, s_k), kn_s[ib]);
+            }
+            qs[ia] = fsub(fmul(q0, cs.x), fmul(q1, cs.y));
+            qs[ib] = fadd(fmul(q0, cs.y), fmul(q1, cs.x));
+            ks[ia] = fsub(fmul(k0, cs.x), fmul(k1, cs.y));
+            ks[ib] = fadd(fmul(k0, cs.y), fmul(k1, cs.x));
         }
         __syncthreads();
         // KV store (ref src/model.c:39-48): the cache holds fp32 or RNE fp16, and
