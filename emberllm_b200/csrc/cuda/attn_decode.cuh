@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnArg
     __shared__ float qs[256], ks[256], vs[256], qn_s[256], kn_s[256];
     __shared__ float2 cs_s[128];
     __shared__ float red[ATTN_THREADS / 32];
-    __shared__ float s_q, s_k, s_max, s_inv;
+    __shared__ float s_q, s_k, s_inv;
     __shared__ double tab_s[64];
     const int h = blockIdx.x, tid = threadIdx.x, hd = a.hd, CH = a.chunk;
     const int kv_mul = a.nh / a.nkv, kvh = h / kv_mul;
