@@ -63,3 +63,38 @@ def test_stream_partition_covers_every_stream():
                 lo, hi = bench.stream_range(total, world, r)
                 seen.extend(range(lo, hi))
             assert seen == list(range(total))
+
+
+def test_streams_summary_reports_the_contract_keys():
+    """the streams aggregate's figures from one measurement: device-timed value,
+    wall-clock e2e with the host copies' bytes, per-stream rate, step time"""
+    sys.path.insert(0, ROOT)
+    import bench
+    m = {"S": 64, "t_wall": 2.0, "t_dev": 1.6, "clk": {}, "gemm": True, "tokens": 512 * 64 * 2}
+    sm = bench.streams_summary(m, 512, 8, 64, 2)
+    assert sm["value"] == round(512 * 64 * 2 / 1.6, 1)
+    assert sm["e2e"]["value"] == round(512 * 64 * 2 / 2.0, 1)
+    assert sm["per_stream_tok_s"] == round(sm["value"] / 512, 2)
+    assert sm["streams"] == 512 and sm["streams_per_gpu"] == 64 and sm["n_gpus"] == 8
+    assert sm["e2e"]["h2d_bytes_per_step"] == 64 * 8 and sm["e2e"]["d2h_bytes_per_step"] == 64 * 64 * 4
+    assert sm["ms_per_step"] == round(1.6 / 2 * 1e3, 3)
+    assert sm["path"] == "batched GEMMs" and "events" in sm["timing"]
+    # without device events (concurrent single-stream states), wall time is the figure
+    m2 = dict(m, t_dev=None, gemm=False)
+    sm2 = bench.streams_summary(m2, 512, 8, 64, 2)
+    assert sm2["value"] == sm2["e2e"]["value"] and sm2["timing"] == "wall clock"
+
+
+def test_streams_partition_has_no_gaps_at_every_scale():
+    """8 x 16, 8 x 64 split over 1..8 GPUs and 64 per GPU: every stream exactly once"""
+    sys.path.insert(0, ROOT)
+    import bench
+    for total_fn in (lambda w: 128, lambda w: 512, lambda w: 64 * w):
+        for world in range(1, 9):
+            total = total_fn(world)
+            seen = []
+            for r in range(world):
+                lo, hi = bench.stream_range(total, world, r)
+                assert hi - lo in (total // world, total // world + 1)
+                seen.extend(range(lo, hi))
+            assert seen == list(range(total))
