@@ -39,6 +39,7 @@ def ref_lib():
     lib.ember_sample.argtypes = [ctypes.POINTER(RefSampler), ctypes.POINTER(ctypes.c_float), ctypes.c_int]
     lib.ember_sampler_accept.argtypes = [ctypes.POINTER(RefSampler), ctypes.c_int]
     lib.ember_sampler_free.argtypes = [ctypes.POINTER(RefSampler)]
+    lib.ember_sampler_reset.argtypes = [ctypes.POINTER(RefSampler)]
     return lib
 
 

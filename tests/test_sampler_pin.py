@@ -35,3 +35,32 @@ def test_oracle_sampler_matches_reference(orc, vocab, k):
         assert tok_o == tok_r, (setting, step)
         assert rng_o == s.rng_state
     ref.ember_sampler_free(s)
+
+
+@pytest.mark.skipif(not H.have_reference(), reason="reference build (oracle/_ref) not present")
+@pytest.mark.parametrize("last_n,rp,pres,freq", [(0, 1.1, 0.0, 0.0), (4, 1.0, 0.0, 0.0), (5, 1.2, 0.3, 0.0),
+                                                  (3, 1.0, 0.0, 0.2), (16, 1.1, 0.5, 0.3)])
+def test_python_sampler_mirrors_the_reference_state(last_n, rp, pres, freq):
+    """emberllm_b200.Sampler (the host half of ember_sample_device) keeps the
+    reference's EmberSampler state: seed handling, a history ring only when a
+    penalty is active, and accept / reset moving hist_len and hist_pos alike"""
+    from emberllm_b200 import Sampler
+    ref = S.ref_lib()
+    for seed in (0, 12345):
+        r = S.RefSampler()
+        ref.ember_sampler_init(S.ctypes.byref(r), 0.7, 0.9, 40, seed)
+        ref.ember_sampler_set_penalties(S.ctypes.byref(r), rp, last_n, pres, freq, 0.05)
+        d = Sampler(0.7, 0.9, 40, seed)
+        d.set_penalties(rp, last_n, pres, freq, 0.05)
+        assert d.rng_state.value == r.rng_state
+        assert (d.history is None) == (not r.history)
+        for step, tok in enumerate([5, 9, 5, 2, 7, 7, 1, 3, 9, 4, 8, 6, 0, 11, 5, 12, 13, 14, 2, 5]):
+            ref.ember_sampler_accept(S.ctypes.byref(r), tok)
+            d.accept(tok)
+            assert (d.hist_len, d.hist_pos) == (r.hist_len, r.hist_pos), step
+            if d.history is not None:
+                assert list(d.history)[:d.hist_len] == [r.history[i] for i in range(r.hist_len)]
+            if step == 9:
+                ref.ember_sampler_reset(S.ctypes.byref(r))
+                d.reset()
+        ref.ember_sampler_free(S.ctypes.byref(r))
